@@ -1,0 +1,46 @@
+// C++ mirror of the reference operator interface
+// (kebab/include/kebab/cuda/cuda_gemm.h:10-33 and the per-version launchers
+// declared at :43-257), implemented over the B200 ladder by libkebab_b200.so.
+// Callers written against the reference compile unchanged: the same
+// baseline::gemm overloads with the same defaults, and the same
+// gemm_cuda_version_feature_name. Like the reference these print an error
+// and return; the status-returning C ABI is in kebab/kebab.h.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "kebab/kebab.h"
+
+namespace baseline {
+
+// Replaces gemm_cuda_version_feature_name (kebab/lib/cuda/cuda_gemm.cu:81-106).
+const char* gemm_cuda_version_feature_name(int version);
+
+// Replace the three overloads at kebab/lib/cuda/cuda_gemm.cu:112, :246, :259.
+// A: M x K, B: K x N, C: M x N column-major; opmode "RC" (A row-major, B
+// column-major). version: a B200 rung (1, 101..105, 120) or a reference id.
+void gemm(const float* A, const float* B, float* C, int M, int N, int K, const char* opmode = "RC",
+          int version = 1, cudaStream_t stream = 0);
+void gemm(const __half* A, const __half* B, __half* C, int M, int N, int K, const char* opmode = "RC",
+          int version = 1, cudaStream_t stream = 0);
+void gemm(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+          const char* opmode = "RC", int version = 1, cudaStream_t stream = 0);
+
+// Per-rung launchers, same argument convention as the reference's
+// gemm_vN_<feature>_fp16(A, B, C, M, N, K, lhs_format, rhs_format, stream).
+#define KEBAB_DECLARE_RUNG(NAME)                                                                          \
+  void NAME##_fp16(const __half* A, const __half* B, __half* C, int M, int N, int K, char lhs_format,    \
+                   char rhs_format, cudaStream_t stream);                                                \
+  void NAME##_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K, \
+                   char lhs_format, char rhs_format, cudaStream_t stream);
+KEBAB_DECLARE_RUNG(gemm_v1_simt_warptiling)                                   // CUDA cores (reference v1)
+KEBAB_DECLARE_RUNG(gemm_v101_tma_mmasync)                                     // TMA staging + mma.sync
+KEBAB_DECLARE_RUNG(gemm_v102_tma_umma_tmem)                                   // + tcgen05.mma, TMEM
+KEBAB_DECLARE_RUNG(gemm_v103_tma_umma_tmem_warpspecialized)                   // + producer/MMA/epilogue warps
+KEBAB_DECLARE_RUNG(gemm_v104_tma_umma_tmem_warpspecialized_persistent)        // + persistent scheduler
+KEBAB_DECLARE_RUNG(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta)   // + cta_group::2 pairs
+#undef KEBAB_DECLARE_RUNG
+
+}  // namespace baseline

@@ -1,0 +1,100 @@
+/*
+ * kebab-b200 C ABI — the drop-in boundary of the B200 GEMM ladder.
+ *
+ * Plain C: pointers, sizes and an opaque stream handle (binary-compatible
+ * with cudaStream_t). All matrix pointers are DEVICE pointers owned by the
+ * caller; A and B are read-only, C is written in full (no alpha/beta). Calls
+ * are asynchronous on `stream` (NULL = legacy default stream) and return a
+ * status code; the message of the last failure on the calling thread is
+ * available from kebab_last_error().
+ *
+ * Layout conventions follow the reference operator (kebab/include/kebab/cuda/
+ * cuda_gemm.h:10-33, kebab/lib/cuda/cuda_gemm.cu:112-303):
+ *   opmode "RC": A is M x K row-major, B is K x N column-major;
+ *   C is M x N column-major (ldC = M); FP32 accumulation.
+ * Indices are int64.
+ */
+#ifndef KEBAB_KEBAB_H_
+#define KEBAB_KEBAB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* kebab_stream_t; /* same type as cudaStream_t */
+
+typedef enum kebab_dtype {
+  KEBAB_F16 = 0,  /* __half (IEEE binary16) */
+  KEBAB_BF16 = 1, /* __nv_bfloat16 */
+  KEBAB_F32 = 2   /* float: accepted by the dispatcher, rejected as ENOTSUP
+                     exactly like baseline::gemm(const float*...) which prints
+                     "not implemented" (cuda_gemm.cu:246-253) */
+} kebab_dtype;
+
+/* Status codes. */
+#define KEBAB_OK 0
+#define KEBAB_EINVAL 22     /* bad pointer, shape, opmode, alignment or version */
+#define KEBAB_ENOTSUP 95    /* valid request this build does not implement */
+#define KEBAB_ECUDA 1001    /* a CUDA runtime/driver call or launch failed */
+#define KEBAB_ETIMEOUT 1002 /* a kernel's bounded wait expired (device status) */
+#define KEBAB_ESPARSE 1003  /* input is not 2:4 sparse (pack step) */
+
+/* Dense GEMM C = A * B through the version ladder.
+ * Replaces baseline::gemm(const T* A, const T* B, T* C, int M, int N, int K,
+ *   const char* opmode, int version, cudaStream_t stream)
+ *   (kebab/lib/cuda/cuda_gemm.cu:112 for __half, :259 for __nv_bfloat16,
+ *   :246 for float), returning a status instead of printing and returning.
+ * `version` is one of the B200 rungs (1, 101..105, 120) or a reference
+ * version id (2..20, 41), which maps to the B200 rung with the same idea
+ * (kebab_version_name() tells which). opmode NULL means "RC". */
+int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+               const char* opmode, int version, kebab_stream_t stream);
+
+/* Name of a version, as used in CSV variant names.
+ * Replaces baseline::gemm_cuda_version_feature_name(int)
+ *   (kebab/lib/cuda/cuda_gemm.cu:81-106); "unknown" for unknown ids. */
+const char* kebab_version_name(int version);
+
+/* The B200 rung a version id resolves to for (dtype, M, N, K), after the
+ * reference-id mapping and, for 120, the decomposition heuristic (the role
+ * of the reference's v20 dispatcher, cuda_gemm.cu:25-77,211-230). Returns the
+ * rung id, or a negative KEBAB_* code. */
+int kebab_resolve_version(int version, kebab_dtype dtype, int64_t M, int64_t N, int64_t K);
+
+/* Fills `out` with the implemented version ids (up to `cap`); returns count. */
+int kebab_list_versions(int* out, int cap);
+
+/* Message of the last failure on this thread ("" if none). No reference
+ * counterpart: the reference prints to stderr (cuda_gemm.cu:115-122). */
+const char* kebab_last_error(void);
+
+/* Reads (and with clear != 0 resets) the device status word that kernels
+ * set when a bounded wait expires. Synchronizes `stream` first. Returns
+ * KEBAB_OK if the word was zero, KEBAB_ETIMEOUT otherwise; *code (optional)
+ * receives the raw word (bits 0..7 class, 8..15 wait site, 16..31 block).
+ * No reference counterpart: the reference's waits spin forever
+ * (cuda_gemm_v10_*:196-209). */
+int kebab_device_status(kebab_stream_t stream, uint32_t* code, int clear);
+
+/* Per-wait budget of every kernel launched afterwards (default 2000 ms, or
+ * the KEBAB_WAIT_TIMEOUT_MS environment variable). */
+int kebab_set_wait_timeout_us(uint64_t timeout_us);
+
+/* Launches a one-warp kernel that waits on an mbarrier nobody arrives at,
+ * with a budget of `timeout_us`; the wait expires and the kernel returns.
+ * Exercises the timeout path without faulting or hanging the GPU. Returns
+ * the status read back afterwards (KEBAB_ETIMEOUT when it works) and clears
+ * it. */
+int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us);
+
+/* Releases cached tensor maps and per-device state. Replaces nothing: the
+ * reference's function-static caches are never freed (cuda_gemm_v10_*:499). */
+void kebab_shutdown(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KEBAB_KEBAB_H_ */

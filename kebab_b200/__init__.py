@@ -1,0 +1,154 @@
+"""kebab_b200 — B200-native (sm_100a) GEMM ladder behind kebab's operator surface.
+
+The product is libkebab_b200.so (kebab_b200/csrc, C ABI in
+include/kebab/kebab.h). This module is the Python mirror of that ABI used by
+the tests and bench.py: it loads the in-tree library with ctypes and passes
+raw device pointers, sizes and the current CUDA stream — PyTorch only
+provides device memory and streams. There is no fallback: if the library is
+missing or a call fails, an exception is raised.
+
+Layout (reference kebab/include/kebab/cuda/cuda_gemm.h:10-33): opmode "RC",
+A is M x K row-major, B is K x N column-major (a torch tensor of shape
+[N, K]), C is M x N column-major (a torch tensor of shape [N, M]).
+"""
+import ctypes
+import os
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "lib", "libkebab_b200.so")
+
+F16, BF16, F32 = 0, 1, 2
+OK, EINVAL, ENOTSUP, ECUDA, ETIMEOUT, ESPARSE = 0, 22, 95, 1001, 1002, 1003
+RUNGS = (1, 101, 102, 103, 104, 105)
+HEURISTIC = 120
+# Reference version ids and the B200 rung each one maps to.
+REFERENCE_ID_MAP = {2: 102, 3: 102, 17: 102, 4: 103, 15: 103, 5: 104, 6: 104, 7: 104, 13: 104, 14: 104,
+                    16: 104, 18: 104, 19: 104, 8: 105, 9: 105, 10: 105, 11: 105, 12: 105, 20: 120}
+
+
+class KebabError(RuntimeError):
+    def __init__(self, code, msg):
+        super().__init__("kebab status %d: %s" % (code, msg))
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """The loaded C ABI (ctypes.CDLL). Raises if the library was not built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise KebabError(ECUDA, "libkebab_b200.so not built: run `python -m kebab_b200.build` "
+                                    "(there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        c = ctypes
+        L.kebab_gemm.argtypes = [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_int64,
+                                 c.c_char_p, c.c_int, c.c_void_p]
+        L.kebab_gemm.restype = c.c_int
+        L.kebab_version_name.argtypes = [c.c_int]
+        L.kebab_version_name.restype = c.c_char_p
+        L.kebab_resolve_version.argtypes = [c.c_int, c.c_int, c.c_int64, c.c_int64, c.c_int64]
+        L.kebab_resolve_version.restype = c.c_int
+        L.kebab_list_versions.argtypes = [c.POINTER(c.c_int), c.c_int]
+        L.kebab_list_versions.restype = c.c_int
+        L.kebab_last_error.argtypes = []
+        L.kebab_last_error.restype = c.c_char_p
+        L.kebab_device_status.argtypes = [c.c_void_p, c.POINTER(c.c_uint32), c.c_int]
+        L.kebab_device_status.restype = c.c_int
+        L.kebab_set_wait_timeout_us.argtypes = [c.c_uint64]
+        L.kebab_set_wait_timeout_us.restype = c.c_int
+        L.kebab_probe_wait_timeout.argtypes = [c.c_void_p, c.c_uint64]
+        L.kebab_probe_wait_timeout.restype = c.c_int
+        L.kebab_shutdown.argtypes = []
+        L.kebab_shutdown.restype = None
+        _lib = L
+    return _lib
+
+
+def last_error():
+    return lib().kebab_last_error().decode()
+
+
+def check(rc):
+    if rc != OK:
+        raise KebabError(rc, last_error())
+    return rc
+
+
+def version_name(version):
+    return lib().kebab_version_name(version).decode()
+
+
+def list_versions():
+    n = lib().kebab_list_versions(None, 0)
+    arr = (ctypes.c_int * n)()
+    lib().kebab_list_versions(arr, n)
+    return list(arr)
+
+
+def _dtype_code(t):
+    import torch
+    if t.dtype == torch.float16:
+        return F16
+    if t.dtype == torch.bfloat16:
+        return BF16
+    if t.dtype == torch.float32:
+        return F32
+    raise KebabError(EINVAL, "unsupported dtype %s" % t.dtype)
+
+
+def _stream_ptr(stream):
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    return ctypes.c_void_p(stream.cuda_stream)
+
+
+def gemm_raw(dtype, a_ptr, b_ptr, c_ptr, M, N, K, opmode="RC", version=HEURISTIC, stream_ptr=None):
+    """Direct C-ABI call with raw device pointers; returns the status code."""
+    return lib().kebab_gemm(dtype, a_ptr, b_ptr, c_ptr, M, N, K, opmode.encode() if opmode else None, version,
+                            stream_ptr)
+
+
+def gemm(A, B, C=None, opmode="RC", version=HEURISTIC, stream=None):
+    """C = A * B in RC mode through kebab_gemm.
+
+    A: [M, K] row-major tensor; B: [N, K] tensor (B column-major, K x N);
+    C: [N, M] tensor (C column-major, M x N), allocated if None. Asynchronous
+    on `stream` (default: torch's current stream). Raises KebabError on a
+    non-zero status."""
+    import torch
+    if A.dim() != 2 or B.dim() != 2:
+        raise KebabError(EINVAL, "A and B must be 2-D")
+    M, K = A.shape
+    N, Kb = B.shape
+    if Kb != K:
+        raise KebabError(EINVAL, "inner dimensions differ: A is %dx%d, B^T is %dx%d" % (M, K, N, Kb))
+    if not (A.is_contiguous() and B.is_contiguous()):
+        raise KebabError(EINVAL, "A and B must be contiguous")
+    if C is None:
+        C = torch.empty((N, M), dtype=A.dtype, device=A.device)
+    elif tuple(C.shape) != (N, M) or not C.is_contiguous():
+        raise KebabError(EINVAL, "C must be a contiguous [N, M] tensor (column-major M x N)")
+    if A.dtype != B.dtype or A.dtype != C.dtype:
+        raise KebabError(EINVAL, "A, B and C must share a dtype")
+    check(gemm_raw(_dtype_code(A), A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, opmode, version,
+                   _stream_ptr(stream)))
+    return C
+
+
+def device_status(stream=None, clear=True):
+    """(status, raw code) of the device status word; synchronizes `stream`."""
+    code = ctypes.c_uint32(0)
+    rc = lib().kebab_device_status(_stream_ptr(stream), ctypes.byref(code), 1 if clear else 0)
+    return rc, code.value
+
+
+def set_wait_timeout_us(us):
+    check(lib().kebab_set_wait_timeout_us(us))
+
+
+def probe_wait_timeout(timeout_us=1000, stream=None):
+    return lib().kebab_probe_wait_timeout(_stream_ptr(stream), timeout_us)

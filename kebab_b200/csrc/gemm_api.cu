@@ -1,0 +1,186 @@
+// Operator surface: the C ABI (kebab_gemm & co.) and the C++ mirror of the
+// reference's baseline:: interface, both dispatching over the B200 ladder.
+//
+// Reference behaviour kept (kebab/lib/cuda/cuda_gemm.cu):
+//   - null pointers / non-positive dims are rejected (:115-122);
+//   - opmode is upper-cased; lhs = opmode[0] or 'R', rhs = opmode[1] or 'C'
+//     (:125-129);
+//   - float inputs are "not implemented" (:246-253);
+//   - unknown versions are rejected (:235-238).
+// Differences: a status code is returned (the C++ overloads still print and
+// return void, like the reference), indices are int64, and reference version
+// ids map onto the B200 rung that carries the same idea.
+#include <algorithm>
+#include <cctype>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "internal.h"
+#include "kebab/cuda/cuda_gemm.h"
+
+namespace kb {
+namespace {
+
+struct Rung {
+  int id;
+  const char* name;
+  int (*launch)(const GemmProblem&);
+};
+
+const Rung kRungs[] = {
+    {1, "simt_warptiling", launch_v1_simt},
+    {101, "tma_mmasync", launch_v101_tma_mmasync},
+    {102, "tma_umma_tmem", launch_v102_umma},
+    {103, "tma_umma_tmem_warpspecialized", launch_v103_ws},
+    {104, "tma_umma_tmem_warpspecialized_persistent", launch_v104_persistent},
+    {105, "tma_umma_tmem_warpspecialized_persistent_2cta", launch_v105_pair},
+};
+
+const Rung* find_rung(int id) {
+  for (const auto& r : kRungs)
+    if (r.id == id) return &r;
+  return nullptr;
+}
+
+// Reference version id -> B200 rung with the same idea (see the table in
+// kebab_version_name's documentation).
+int map_reference_id(int v) {
+  switch (v) {
+    case 2: case 3: case 17: return 102;             // TMA + one MMA stream per CTA
+    case 4: case 15: return 103;                     // warp specialised, one tile per CTA
+    case 5: case 6: case 7: case 13: case 14:
+    case 16: case 18: case 19: return 104;           // persistent scheduler
+    case 8: case 9: case 10: case 11: case 12: return 105;  // cluster pairs
+    case 20: return 120;                             // decomposition heuristic
+    default: return v;
+  }
+}
+
+// The role of the reference's v20 heuristic (cuda_gemm.cu:25-77): choose a
+// decomposition from the tile count against the QUERIED SM count.
+// KEBAB_V120_MODE = dp | persistent | pair | heuristic (default).
+int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count) {
+  const char* env = std::getenv("KEBAB_V120_MODE");
+  if (env && *env) {
+    std::string m(env);
+    std::transform(m.begin(), m.end(), m.begin(), [](unsigned char c) { return (char)std::toupper(c); });
+    if (m == "DP" || m == "DATAPARALLEL") return 103;
+    if (m == "PERSISTENT") return 104;
+    if (m == "PAIR" || m == "2CTA") return 105;
+  }
+  const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
+  if (pair_tiles >= sm_count / 2) return 105;
+  return 104;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" {
+
+const char* kebab_version_name(int version) {
+  if (version == 120) return "decomposition_heuristic";
+  const int id = map_reference_id(version);
+  if (id == 120) return "decomposition_heuristic";
+  const Rung* r = find_rung(id);
+  return r ? r->name : "unknown";
+}
+
+int kebab_list_versions(int* out, int cap) {
+  int n = 0;
+  for (const auto& r : kRungs)
+    if (out && n < cap) out[n++] = r.id; else if (!out) ++n;
+  if (out && n < cap) out[n++] = 120;
+  else if (!out) ++n;
+  return n;
+}
+
+int kebab_resolve_version(int version, kebab_dtype dtype, int64_t M, int64_t N, int64_t K) {
+  (void)dtype;
+  int id = map_reference_id(version);
+  if (id == 120) {
+    DeviceInfo* d = nullptr;
+    int rc = device_info(&d);
+    int sms = rc == KEBAB_OK ? d->sm_count : 148;
+    id = choose_v120(M, N, K, sms);
+  }
+  if (!find_rung(id)) {
+    fail(KEBAB_EINVAL, "unsupported version " + std::to_string(version));
+    return -KEBAB_EINVAL;
+  }
+  return id;
+}
+
+int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+               const char* opmode, int version, kebab_stream_t stream) {
+  if (!A || !B || !C) return fail(KEBAB_EINVAL, "null pointer passed to kebab_gemm");
+  if (M <= 0 || N <= 0 || K <= 0)
+    return fail(KEBAB_EINVAL, "invalid dimensions: M=" + std::to_string(M) + ", N=" + std::to_string(N) +
+                                  ", K=" + std::to_string(K));
+  if (dtype == KEBAB_F32) return fail(KEBAB_ENOTSUP, "float precision not implemented; use half or bfloat16");
+  if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "unknown dtype");
+  std::string mode(opmode ? opmode : "RC");
+  std::transform(mode.begin(), mode.end(), mode.begin(), [](unsigned char c) { return (char)std::toupper(c); });
+  const char lhs = mode.size() >= 1 ? mode[0] : 'R';
+  const char rhs = mode.size() >= 2 ? mode[1] : 'C';
+  if ((lhs != 'R' && lhs != 'C') || (rhs != 'R' && rhs != 'C'))
+    return fail(KEBAB_EINVAL, "opmode must be two of R/C, got \"" + mode + "\"");
+  const int id = kebab_resolve_version(version, dtype, M, N, K);
+  if (id < 0) return -id;
+  const Rung* r = find_rung(id);
+  GemmProblem p{(int)dtype, A, B, C, M, N, K, lhs, rhs, reinterpret_cast<cudaStream_t>(stream)};
+  return r->launch(p);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// C++ mirror of the reference interface (kebab/include/kebab/cuda/cuda_gemm.h)
+// ---------------------------------------------------------------------------
+namespace baseline {
+
+const char* gemm_cuda_version_feature_name(int version) { return kebab_version_name(version); }
+
+static void report(int rc, const char* what) {
+  if (rc != KEBAB_OK) std::fprintf(stderr, "ERROR: %s: %s\n", what, kebab_last_error());
+}
+
+void gemm(const float* A, const float* B, float* C, int M, int N, int K, const char* opmode, int version,
+          cudaStream_t stream) {
+  report(kebab_gemm(KEBAB_F32, A, B, C, M, N, K, opmode, version, stream), "baseline::gemm (float)");
+}
+void gemm(const __half* A, const __half* B, __half* C, int M, int N, int K, const char* opmode, int version,
+          cudaStream_t stream) {
+  report(kebab_gemm(KEBAB_F16, A, B, C, M, N, K, opmode, version, stream), "baseline::gemm (half)");
+}
+void gemm(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,
+          const char* opmode, int version, cudaStream_t stream) {
+  report(kebab_gemm(KEBAB_BF16, A, B, C, M, N, K, opmode, version, stream), "baseline::gemm (bfloat16)");
+}
+
+#define KEBAB_RUNG_LAUNCHER(NAME, ID)                                                                            \
+  void NAME##_fp16(const __half* A, const __half* B, __half* C, int M, int N, int K, char lhs_format,          \
+                   char rhs_format, cudaStream_t stream) {                                                     \
+    const char mode[3] = {lhs_format, rhs_format, 0};                                                          \
+    report(kebab_gemm(KEBAB_F16, A, B, C, M, N, K, mode, ID, stream), #NAME "_fp16");                         \
+  }                                                                                                            \
+  void NAME##_bf16(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,      \
+                   char lhs_format, char rhs_format, cudaStream_t stream) {                                    \
+    const char mode[3] = {lhs_format, rhs_format, 0};                                                          \
+    report(kebab_gemm(KEBAB_BF16, A, B, C, M, N, K, mode, ID, stream), #NAME "_bf16");                        \
+  }
+
+KEBAB_RUNG_LAUNCHER(gemm_v1_simt_warptiling, 1)
+KEBAB_RUNG_LAUNCHER(gemm_v101_tma_mmasync, 101)
+KEBAB_RUNG_LAUNCHER(gemm_v102_tma_umma_tmem, 102)
+KEBAB_RUNG_LAUNCHER(gemm_v103_tma_umma_tmem_warpspecialized, 103)
+KEBAB_RUNG_LAUNCHER(gemm_v104_tma_umma_tmem_warpspecialized_persistent, 104)
+KEBAB_RUNG_LAUNCHER(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta, 105)
+#undef KEBAB_RUNG_LAUNCHER
+
+}  // namespace baseline

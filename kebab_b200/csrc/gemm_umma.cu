@@ -1,0 +1,109 @@
+// Launchers of the warp-specialised tcgen05 rungs (v103, v104, v105).
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_umma.cuh"
+#include "internal.h"
+
+namespace kb {
+
+namespace {
+
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT>
+int launch_umma(const GemmProblem& p) {
+  using L = UmmaSmem<BN, STAGES, CG>;
+  int rc = check_tma_shapes(p);
+  if (rc) return rc;
+  if (p.lhs != 'R' || p.rhs != 'C') return fail(KEBAB_ENOTSUP, "this rung implements opmode RC only");
+  DeviceInfo* dev = nullptr;
+  if ((rc = device_info(&dev))) return rc;
+  UmmaArgs args;
+  if ((rc = wait_ctx(&args.ctx))) return rc;
+
+  constexpr int BM_T = 128 * CG;
+  CUtensorMap tA, tB, tC;
+  // A: M x K row-major; box = 128 rows x 64 K (one CTA's half of a pair tile).
+  if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.M, p.K, p.K, 128, 64, true))) return rc;
+  // B: column-major K x N = row-major N x K; box = BN/CG columns x 64 K.
+  if ((rc = make_tmap_2d(&tB, p.B, p.dtype, p.N, p.K, p.K, BN / CG, 64, true))) return rc;
+  // C: column-major M x N = row-major N x M; box = 32 columns x 32 rows.
+  if ((rc = make_tmap_2d(&tC, p.C, p.dtype, p.N, p.M, p.M, 32, 32, false))) return rc;
+
+  args.M = (int)p.M;
+  args.N = (int)p.N;
+  args.K = (int)p.K;
+  args.tiles_m = (int)((p.M + BM_T - 1) / BM_T);
+  args.tiles_n = (int)((p.N + BN - 1) / BN);
+  args.group_m = 16;
+  const long long tiles = (long long)args.tiles_m * args.tiles_n;
+  if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
+
+  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT>;
+  static std::once_flag attr_once[64];
+  static cudaError_t attr_err[64];
+  const int di = dev->device & 63;
+  std::call_once(attr_once[di], [&] {
+    attr_err[di] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  });
+  if (attr_err[di] != cudaSuccess) return cuda_fail(attr_err[di], "cudaFuncSetAttribute(max dynamic smem)");
+
+  int clusters;
+  if (PERSISTENT) {
+    int max_clusters = dev->sm_count / CG;
+    if (CG > 1) {
+      // Pairs must be co-resident on a GPC; ask the occupancy API how many fit.
+      static int max_active[64] = {0};
+      if (max_active[di] == 0) {
+        cudaLaunchConfig_t qc = {};
+        qc.gridDim = dim3(CG * max_clusters, 1, 1);
+        qc.blockDim = dim3(192, 1, 1);
+        qc.dynamicSmemBytes = L::ALLOC;
+        cudaLaunchAttribute qa[1];
+        qa[0].id = cudaLaunchAttributeClusterDimension;
+        qa[0].val.clusterDim.x = CG;
+        qa[0].val.clusterDim.y = 1;
+        qa[0].val.clusterDim.z = 1;
+        qc.attrs = qa;
+        qc.numAttrs = 1;
+        int n = 0;
+        cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
+        max_active[di] = (e == cudaSuccess && n > 0) ? n : max_clusters;
+        (void)cudaGetLastError();
+      }
+      max_clusters = std::min(max_clusters, max_active[di]);
+    }
+    clusters = (int)std::min<long long>(tiles, max_clusters);
+  } else {
+    clusters = (int)tiles;
+  }
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CG * clusters, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = p.stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, args);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_umma_ws launch");
+  return KEBAB_OK;
+}
+
+template <int CG, bool PERSISTENT, int STAGES>
+int dispatch_dtype(const GemmProblem& p) {
+  if (p.dtype == KEBAB_F16) return launch_umma<__half, 256, STAGES, CG, PERSISTENT>(p);
+  return launch_umma<__nv_bfloat16, 256, STAGES, CG, PERSISTENT>(p);
+}
+
+}  // namespace
+
+int launch_v103_ws(const GemmProblem& p) { return dispatch_dtype<1, false, 4>(p); }
+int launch_v104_persistent(const GemmProblem& p) { return dispatch_dtype<1, true, 4>(p); }
+int launch_v105_pair(const GemmProblem& p) { return dispatch_dtype<2, true, 6>(p); }
+
+}  // namespace kb

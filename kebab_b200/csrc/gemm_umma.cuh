@@ -1,0 +1,309 @@
+// Warp-specialised tcgen05 GEMM (the v103 / v104 / v105 rungs of the ladder).
+//
+// C (M x N, column-major, ldC = M) = A (M x K, row-major) * B (K x N,
+// column-major), FP16 or BF16 inputs, FP32 accumulation in TMEM, FP16/BF16
+// output. This is the sm_100a replacement for the reference's warp-
+// specialised WGMMA kernels (kebab/lib/cuda/cuda_gemm_v4_* ... v19_*, hot loop
+// described at cuda_gemm_v10_*:313-473): same operator, different machine.
+//
+// Roles (192 threads, 6 warps):
+//   warp 0        TMA producer: one elected lane streams K-blocks of A and B
+//                 into a STAGES-deep shared-memory ring (128-byte swizzle).
+//   warp 1        TMEM owner + MMA issuer: allocates 512 TMEM columns (two
+//                 BN-column FP32 accumulators), one lane issues
+//                 tcgen05.mma (kind::f16, 128 x BN x 16, or 256 x BN x 16 over
+//                 a CTA pair) and tcgen05.commit to release ring slots.
+//   warps 2..5    epilogue: tcgen05.ld 32 columns at a time, convert, stage
+//                 32 x 32 column-major sub-tiles in shared memory and write
+//                 them with TMA stores; the accumulator is released as soon
+//                 as it has been read, so the next tile's MMAs overlap the
+//                 stores.
+// Template knobs, one per rung:
+//   PERSISTENT=false  grid = #tiles, one tile per CTA                 (v103)
+//   PERSISTENT=true   grid = #SMs, static grouped-raster schedule,
+//                     double-buffered accumulators                     (v104)
+//   CG=2              CTA pairs (cluster 2x1), tcgen05 cta_group::2,
+//                     256 x BN tiles; each CTA TMA-loads its own half of
+//                     A (rows) and of B (columns) — no multicast loads  (v105)
+// Every barrier wait is bounded (ptx.cuh); on expiry the kernel records an
+// error code, drains what it has in flight and returns.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace kb {
+
+template <typename T>
+struct ElemTraits;
+template <>
+struct ElemTraits<__half> {
+  static constexpr int kBf16 = 0;
+  __device__ static __forceinline__ __half cvt(float v) { return __float2half_rn(v); }
+};
+template <>
+struct ElemTraits<__nv_bfloat16> {
+  static constexpr int kBf16 = 1;
+  __device__ static __forceinline__ __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
+};
+
+// Grouped rasterisation: consecutive tile ids walk down `group_m` M-blocks
+// before moving to the next N-block, so concurrently running CTAs share A
+// rows and B columns in L2.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int group_m, int& mb, int& nb) {
+  const int group_size = group_m * tiles_n;
+  const int g = tile / group_size;
+  const int first_m = g * group_m;
+  const int gm = min(group_m, tiles_m - first_m);
+  const int r = tile - g * group_size;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+struct UmmaArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, group_m;
+  WaitCtx ctx;
+};
+
+template <int BN, int STAGES, int CG>
+struct UmmaSmem {
+  static constexpr int BM = 128;  // rows of A per CTA
+  static constexpr int BK = 64;   // 64 x 2 bytes = one 128-byte swizzle row
+  static constexpr int A_STAGE = BM * BK * 2;
+  static constexpr int B_STAGE = (BN / CG) * BK * 2;
+  static constexpr int C_SUB = 32 * 32 * 2;  // one 32x32 staging sub-tile
+  static constexpr int C_BYTES = 4 * 2 * C_SUB;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
+  static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
+  static constexpr int OFF_BAR = OFF_C + C_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+  static constexpr int BYTES = OFF_BAR + NUM_BARS * 8 + 16;
+  static constexpr int ALLOC = BYTES + 1024;  // slack for 1024-byte alignment
+  static_assert(BYTES + 1024 <= 232448, "shared memory budget exceeded");
+};
+
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT>
+__global__ void __launch_bounds__(192, 1)
+    gemm_umma_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const UmmaArgs args) {
+  using L = UmmaSmem<BN, STAGES, CG>;
+  constexpr int BM_T = 128 * CG;  // rows per (pair) tile
+  constexpr int TMEM_COLS = 512;
+  constexpr uint32_t IDESC = umma_idesc_f16(BM_T, BN, ElemTraits<T>::kBf16);
+  constexpr uint32_t TX_BYTES = (L::A_STAGE + L::B_STAGE) * CG;  // bytes landing on the issuing CTA's barrier
+  static_assert(2 * BN <= TMEM_COLS, "two accumulators must fit in TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tmem_full = bars + 2 * STAGES;
+  uint64_t* tmem_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NUM_BARS);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = (rank == 0);
+  const WaitCtx& ctx = args.ctx;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4 * CG);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(tmem_slot, TMEM_COLS);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int cluster_id = blockIdx.x / CG;
+  const int num_clusters = gridDim.x / CG;
+  const int tile_step = PERSISTENT ? num_clusters : num_tiles;  // non-persistent: exactly one tile
+  const int num_kb = (args.K + L::BK - 1) / L::BK;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      uint32_t issued_parity[STAGES];
+      bool issued[STAGES];
+      for (int s = 0; s < STAGES; ++s) issued[s] = false;
+      const uint32_t full_leader0 = (CG == 2) ? mapa_shared(smem_u32(&full[0]), 0) : 0u;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += tile_step) {
+        int mb, nb;
+        tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+        const int m0 = mb * BM_T + (int)rank * 128;
+        const int n0 = nb * BN + (int)rank * (BN / CG);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, ctx, SITE_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + L::OFF_A + stage * L::A_STAGE;
+          uint8_t* sB = smem + L::OFF_B + stage * L::B_STAGE;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+            tma_load_2d(sA, &tmA, &full[stage], kb * L::BK, m0);
+            tma_load_2d(sB, &tmB, &full[stage], kb * L::BK, n0);
+          } else {
+            if (leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+            const uint32_t fb = full_leader0 + stage * 8u;
+            tma_load_2d_pair(sA, &tmA, fb, kb * L::BK, m0);
+            tma_load_2d_pair(sB, &tmB, fb, kb * L::BK, n0);
+          }
+          issued[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok && (CG == 1 || leader)) {
+        // Abort: let our own copies still in flight land before the CTA exits.
+        WaitCtx drain_ctx{ctx.status, 50000000ull};
+        for (int s = 0; s < STAGES; ++s)
+          if (issued[s]) mbar_wait(&full[s], issued_parity[s], drain_ctx, SITE_DRAIN);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------- MMA issuer
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool any_issued = false;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += tile_step) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
+          const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
+#pragma unroll
+          for (int k = 0; k < L::BK / 16; ++k) {
+            const uint64_t ad = umma_desc_sw128(a_addr + k * 32);
+            const uint64_t bd = umma_desc_sw128(b_addr + k * 32);
+            if constexpr (CG == 1)
+              umma_f16_cg1(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            else
+              umma_f16_cg2(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          any_issued = true;
+          if constexpr (CG == 1) umma_commit_cg1(&empty[stage]);
+          else umma_commit_cg2_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if constexpr (CG == 1) umma_commit_cg1(&tmem_full[acc]);
+        else umma_commit_cg2_mc(&tmem_full[acc], 0x3);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok && any_issued) {
+        // Abort: wait for the MMAs already issued before TMEM is freed.
+        if constexpr (CG == 1) umma_commit_cg1(drain);
+        else umma_commit_cg2_mc(drain, 0x1);
+        WaitCtx drain_ctx{ctx.status, 50000000ull};
+        mbar_wait(drain, 0, drain_ctx, SITE_DRAIN);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int q = warp & 3;       // TMEM lane quarter this warp may access
+    const int ew = warp - 2;      // epilogue warp index 0..3 (staging buffers)
+    T* stage_c = reinterpret_cast<T*>(smem + L::OFF_C + ew * 2 * L::C_SUB);
+    const uint32_t tmem_empty_leader0 = (CG == 2) ? mapa_shared(smem_u32(&tmem_empty[0]), 0) : 0u;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sub = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += tile_step) {
+      int mb, nb;
+      tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+      const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
+      const int n0 = nb * BN;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), v);
+        tmem_ld_wait();
+        if (c == BN / 32 - 1) {
+          // Accumulator fully read: hand it back to the MMA issuer.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1) mbar_arrive(&tmem_empty[acc]);
+            else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
+          }
+        }
+        T* buf = stage_c + (sub & 1) * (32 * 32);
+        if (lane == 0) tma_store_wait_read<1>();  // the store that used `buf` has read it
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
+          tma_store_commit();
+        }
+        ++sub;
+      }
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  // ------------------------------------------------------------- teardown
+  __syncwarp();
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace kb

@@ -1,0 +1,61 @@
+// Internal host-side declarations shared by the translation units of
+// libkebab_b200.so (not part of the public interface in include/).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "kebab/kebab.h"
+#include "ptx.cuh"
+
+namespace kb {
+
+// Thread-local last-error message behind kebab_last_error().
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+
+// Per-device runtime facts, queried once per device.
+struct DeviceInfo {
+  int device = -1;
+  int sm_count = 0;
+  int cc_major = 0, cc_minor = 0;
+  uint32_t* status = nullptr;  // device address of the status word
+};
+int device_info(DeviceInfo** out);  // for the current device
+
+// Wait context for kernels launched now (status word + current timeout).
+int wait_ctx(WaitCtx* out);
+
+// 2D tensor map over a row-major [rows][cols] array of 2-byte elements
+// (cols contiguous, row pitch `ld` elements), box {box_cols, box_rows}.
+// swizzle128: 128-byte swizzle (box_cols * 2 must be 128).
+int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+
+// Problem description passed to every launcher.
+struct GemmProblem {
+  int dtype;  // KEBAB_F16 / KEBAB_BF16
+  const void* A;
+  const void* B;
+  void* C;
+  int64_t M, N, K;
+  char lhs, rhs;  // 'R'/'C' storage of A and B
+  cudaStream_t stream;
+};
+
+// Launchers of the ladder rungs (return KEBAB_* status).
+int launch_v1_simt(const GemmProblem& p);
+int launch_v101_tma_mmasync(const GemmProblem& p);
+int launch_v102_umma(const GemmProblem& p);
+int launch_v103_ws(const GemmProblem& p);
+int launch_v104_persistent(const GemmProblem& p);
+int launch_v105_pair(const GemmProblem& p);
+
+// Validation shared by the TMA-based rungs: 16-byte aligned pointers and
+// row pitches (K % 8 == 0 for A/B rows, M % 8 == 0 for C columns).
+int check_tma_shapes(const GemmProblem& p);
+
+}  // namespace kb

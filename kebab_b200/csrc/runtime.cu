@@ -1,0 +1,209 @@
+// Host runtime of libkebab_b200.so: error plumbing, per-device state (SM
+// count, the device status word), TMA descriptor encoding, the wait-timeout
+// probe kernel.
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "internal.h"
+
+namespace kb {
+
+// Status word that kernels set when a bounded wait expires. One per device
+// (a __device__ variable is instantiated in every context that loads the
+// module); kernels receive its address as a parameter.
+__device__ uint32_t g_device_status_word;
+
+namespace {
+thread_local std::string t_last_error;
+std::mutex g_mu;
+std::vector<DeviceInfo*> g_devices;
+uint64_t g_timeout_ns = 0;  // 0 = not yet initialised
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+uint64_t default_timeout_ns() {
+  const char* e = std::getenv("KEBAB_WAIT_TIMEOUT_MS");
+  if (e && *e) {
+    long long ms = std::atoll(e);
+    if (ms > 0) return (uint64_t)ms * 1000000ull;
+  }
+  return 2000ull * 1000000ull;
+}
+}  // namespace
+
+void set_error(const std::string& msg) { t_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(KEBAB_ECUDA, std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_mu);
+  if ((int)g_devices.size() <= dev) g_devices.resize(dev + 1, nullptr);
+  if (!g_devices[dev]) {
+    auto* d = new DeviceInfo();
+    d->device = dev;
+    if ((e = cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d->cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&d->cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) {
+      delete d;
+      return cuda_fail(e, "cudaDeviceGetAttribute");
+    }
+    void* p = nullptr;
+    if ((e = cudaGetSymbolAddress(&p, g_device_status_word)) != cudaSuccess) {
+      delete d;
+      return cuda_fail(e, "cudaGetSymbolAddress(status word)");
+    }
+    d->status = static_cast<uint32_t*>(p);
+    g_devices[dev] = d;
+  }
+  *out = g_devices[dev];
+  if ((*out)->cc_major != 10) {
+    return fail(KEBAB_ENOTSUP, "kebab-b200 kernels are built for sm_100a only; device " + std::to_string(dev) +
+                                   " is sm_" + std::to_string((*out)->cc_major) + std::to_string((*out)->cc_minor));
+  }
+  return KEBAB_OK;
+}
+
+int wait_ctx(WaitCtx* out) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g_timeout_ns == 0) g_timeout_ns = default_timeout_ns();
+    out->timeout_ns = g_timeout_ns;
+  }
+  out->status = d->status;
+  return KEBAB_OK;
+}
+
+static int get_encoder() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_encode) return KEBAB_OK;
+  void* fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+    return fail(KEBAB_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  return KEBAB_OK;
+}
+
+int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  int rc = get_encoder();
+  if (rc) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    return fail(KEBAB_EINVAL, "TMA operand base address is not 16-byte aligned");
+  if ((ld * 2) % 16 != 0) return fail(KEBAB_EINVAL, "TMA operand row pitch is not a multiple of 16 bytes");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType t = dtype == KEBAB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = g_encode(out, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(KEBAB_EINVAL, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
+  return KEBAB_OK;
+}
+
+int check_tma_shapes(const GemmProblem& p) {
+  if ((reinterpret_cast<uintptr_t>(p.A) | reinterpret_cast<uintptr_t>(p.B) | reinterpret_cast<uintptr_t>(p.C)) & 15u)
+    return fail(KEBAB_EINVAL, "A, B and C must be 16-byte aligned for the TMA rungs");
+  if (p.K % 8 != 0) return fail(KEBAB_EINVAL, "K must be a multiple of 8 (16-byte rows of A and B) for the TMA rungs");
+  if (p.M % 8 != 0) return fail(KEBAB_EINVAL, "M must be a multiple of 8 (16-byte columns of C) for the TMA rungs");
+  if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX)
+    return fail(KEBAB_EINVAL, "each of M, N, K must fit in int32 for the TMA rungs");
+  return KEBAB_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Deliberate-timeout probe: one warp waits on an mbarrier that nothing will
+// ever arrive at; the bounded wait expires, records the error and returns.
+// ---------------------------------------------------------------------------
+__global__ void probe_wait_kernel(WaitCtx ctx) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, ctx, SITE_PROBE);
+  __syncthreads();
+}
+
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" {
+
+const char* kebab_last_error(void) { return t_last_error.c_str(); }
+
+int kebab_set_wait_timeout_us(uint64_t timeout_us) {
+  if (timeout_us == 0) return fail(KEBAB_EINVAL, "timeout must be positive");
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_timeout_ns = timeout_us * 1000ull;
+  return KEBAB_OK;
+}
+
+int kebab_device_status(kebab_stream_t stream, uint32_t* code, int clear) {
+  DeviceInfo* d = nullptr;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t w = 0;
+  if ((e = cudaMemcpy(&w, d->status, sizeof(w), cudaMemcpyDeviceToHost)) != cudaSuccess)
+    return cuda_fail(e, "reading the device status word");
+  if (code) *code = w;
+  if (clear && w) {
+    uint32_t z = 0;
+    if ((e = cudaMemcpy(d->status, &z, sizeof(z), cudaMemcpyHostToDevice)) != cudaSuccess)
+      return cuda_fail(e, "clearing the device status word");
+  }
+  if (w) {
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "device wait timed out: class %u, site %u, block %u", w & 0xFFu, (w >> 8) & 0xFFu,
+                  w >> 16);
+    return fail(KEBAB_ETIMEOUT, buf);
+  }
+  return KEBAB_OK;
+}
+
+int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us) {
+  WaitCtx ctx;
+  int rc = wait_ctx(&ctx);
+  if (rc) return rc;
+  // Start from a clean word so the result reflects this probe only.
+  rc = kebab_device_status(stream, nullptr, 1);
+  if (rc != KEBAB_OK && rc != KEBAB_ETIMEOUT) return rc;
+  ctx.timeout_ns = timeout_us * 1000ull;
+  probe_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(ctx);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "probe launch");
+  return kebab_device_status(stream, nullptr, 1);
+}
+
+void kebab_shutdown(void) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (auto* d : g_devices) delete d;
+  g_devices.clear();
+}
+
+}  // extern "C"

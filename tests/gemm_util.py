@@ -1,0 +1,52 @@
+"""Helpers shared by the GPU parity tests: seeded inputs from the oracle's
+generators, upload to the device, run a rung through the C ABI, compare with
+the CPU oracle under the north-star tolerance."""
+import numpy as np
+
+import oracle as O
+
+TOL_REL_FRO = 1e-3  # ||C_dev - C_ref||_F / ||C_ref||_F
+TOL_ELEM = 1e-2     # |C_dev - C_ref| <= 1e-2 * (1 + |C_ref|) elementwise
+
+
+def torch_dtype(dt):
+    import torch
+    return torch.float16 if dt == O.F16 else torch.bfloat16
+
+
+def inputs(M, N, K, seed=0, dtype=O.F16, dist=O.NORMAL, scale_a=None, scale_b=None):
+    if dist == O.NORMAL:
+        scale_a = 1.0 / np.sqrt(K) if scale_a is None else scale_a
+        scale_b = 1.0 / np.sqrt(K) if scale_b is None else scale_b
+    else:
+        scale_a = 1.0 if scale_a is None else scale_a
+        scale_b = 1.0 if scale_b is None else scale_b
+    return O.fill_pair(M, N, K, seed=seed, dtype=dtype, dist=dist, scale_a=scale_a, scale_b=scale_b)
+
+
+def to_device(bits, shape, dtype, device):
+    import torch
+    t = torch.from_numpy(bits.view(np.int16).reshape(shape)).to(device)
+    return t.view(torch_dtype(dtype))
+
+
+def run(A_bits, B_bits, M, N, K, dtype, version, device, poison=True):
+    """Runs kebab_gemm; returns C as a flat float32 column-major numpy array."""
+    import torch
+    import kebab_b200 as kb
+    A = to_device(A_bits, (M, K), dtype, device)
+    B = to_device(B_bits, (N, K), dtype, device)
+    C = torch.empty((N, M), dtype=torch_dtype(dtype), device=device)
+    if poison:
+        C.fill_(float("nan"))
+    kb.gemm(A, B, C, version=version)
+    torch.cuda.synchronize()
+    rc, code = kb.device_status()
+    assert rc == kb.OK, "device status 0x%x" % code
+    return C.float().cpu().numpy().reshape(-1)
+
+
+def assert_close(c_dev, c_ref, what=""):
+    ok, rel, worst = O.check_tolerance(c_dev, c_ref, TOL_REL_FRO, TOL_ELEM)
+    assert ok, "%s: rel_fro=%.3e worst_elem_ratio=%.3f nan=%d" % (what, rel, worst, int(np.isnan(c_dev).sum()))
+    return rel, worst
