@@ -1,0 +1,425 @@
+"""Benchmark of the kebab-b200 GEMM path (one JSON line on rank 0).
+
+Workload (M=N=K=8192 FP16 RC, N(0,1)/sqrt(K) inputs),
+M-sharded across ranks with WEAK scaling: every rank owns an 8192-row block
+of A (global M = 8192 * world), B (8192 x 8192, column-major) is broadcast
+once from rank 0 over NCCL before timing (the broadcast is timed on its own
+and reported as `broadcast_ms`), and each rank writes its own column-major C
+shard. A step is one kebab_gemm launch per rank. With N=1 this is exactly the
+single-GPU 8192^3 headline.
+
+Timing: W warm-up steps, then K timed steps between a barrier + synchronize
+on both sides, CUDA events on the launching stream, max over ranks. Three
+rotating input sets (3 x 256 MiB of A + B per rank, > 126 MB L2) keep
+consecutive steps from hitting inputs left in L2 by the previous step.
+
+`--impl reference` times the reference's own CPU GEMM (referenceGemmCpp
+<float> compiled from the reference sources into oracle/_ref, one row block
+per host thread) on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "FP16 RC GEMM TFLOP/s @ M=N=K=8192, % of B200 dense peak; 1/2/4/8-GPU aggregate"
+UNIT = "TFLOP/s"
+NOMINAL_DENSE_TFLOPS = 2250.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", default="kebab", choices=["kebab", "reference"])
+    p.add_argument("--version", type=int, default=120, help="ladder rung (120 = heuristic)")
+    p.add_argument("--m", type=int, default=8192, help="rows of A per rank")
+    p.add_argument("--n", type=int, default=8192)
+    p.add_argument("--k", type=int, default=8192)
+    p.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    p.add_argument("--e2e-steps", type=int, default=5)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-cublas", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work for the cpu_baseline sample")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return {"bf16_tflops": float(d["bf16_tflops"]), "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]),
+                "hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def load_traffic(workload):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            d = json.load(f)
+        return d.get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS, "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sms:
+            return None
+        return {"sm_mhz": float(np.median(sms)), "sm_max_mhz": float(max(maxes)), "reasons": sorted(reasons),
+                "samples": len(sms)}
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def make_inputs(torch, M, N, K, dtype, device, seed):
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    s = 1.0 / np.sqrt(K)
+    A = (torch.randn((M, K), generator=g, device=device, dtype=torch.float32) * s).to(dtype)
+    B = (torch.randn((N, K), generator=g, device=device, dtype=torch.float32) * s).to(dtype)
+    return A, B
+
+
+def cpu_baseline_port(M, N, K, target_s):
+    """The oracle restatement (bit-identical to referenceGemmCpp<float>) on all
+    host cores over a bounded row sample of the workload."""
+    import oracle as O
+    threads = cpu_threads()
+    A, B = O.fill_pair(min(M, 256), N, K, seed=0, dtype=O.F16, dist=O.NORMAL, scale_a=1 / np.sqrt(K),
+                       scale_b=1 / np.sqrt(K))
+    Mp = min(M, 256)
+    rows = np.arange(0, min(Mp, threads), dtype=np.int64)
+    t0 = time.perf_counter()
+    O.gemm_rows(A, B, rows, Mp, N, K, O.F16, threads)
+    dt = time.perf_counter() - t0
+    n_rows = int(max(len(rows), min(Mp, round(len(rows) * target_s / max(dt, 1e-3)))))
+    rows = np.arange(n_rows, dtype=np.int64) % Mp
+    t0 = time.perf_counter()
+    O.gemm_rows(A, B, rows, Mp, N, K, O.F16, threads)
+    dt = time.perf_counter() - t0
+    flops = 2.0 * n_rows * N * K
+    return {"value": flops / dt / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": "%d rows x %d cols of C (K=%d) of the %dx%dx%d workload, %.1f s" % (n_rows, N, K, M, N, K, dt)}
+
+
+class RefCpuGemm:
+    """referenceGemmCpp<float> (compiled from the reference sources into
+    oracle/_ref) over row blocks, one block per host thread."""
+
+    def __init__(self, N, K, threads, rows_per_thread):
+        import oracle as O
+        self.L = O.ref()
+        if self.L is None:
+            raise RuntimeError("oracle/_ref/libkebab_ref.so not built")
+        self.N, self.K, self.threads, self.rpt = N, K, threads, rows_per_thread
+        rows = threads * rows_per_thread
+        A, B = O.fill_pair(rows, N, K, seed=0, dtype=O.F16, dist=O.NORMAL, scale_a=1 / np.sqrt(K),
+                           scale_b=1 / np.sqrt(K))
+        self.A = O.to_float(A, O.F16).reshape(rows, K)
+        self.B = np.ascontiguousarray(O.to_float(B, O.F16))
+        self.C = [np.empty(rows_per_thread * N, np.float32) for _ in range(threads)]
+
+    def step(self):
+        def work(t):
+            a = np.ascontiguousarray(self.A[t * self.rpt:(t + 1) * self.rpt].reshape(-1))
+            self.L.kbr_gemm_f32(a, self.B, self.C[t], self.rpt, self.N, self.K)
+        ts = [threading.Thread(target=work, args=(t,)) for t in range(self.threads)]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join()
+        return 2.0 * self.threads * self.rpt * self.N * self.K
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = cpu_threads()
+    M, N, K = args.m, args.n, args.k
+    workload = "gemm_rc_%s_%dx%dx%d_msharded" % (args.dtype, M, N, K)
+    try:
+        ref = RefCpuGemm(N, K, threads, 1)
+    except Exception as e:
+        print(json.dumps({"impl": "reference", "unavailable": "reference CPU GEMM not built: %s" % e}))
+        return
+    # Size one step at ~2 s of CPU work so warm-up + steps stay within minutes.
+    t0 = time.perf_counter()
+    ref.step()
+    dt1 = time.perf_counter() - t0
+    rpt = max(1, min(64, int(2.0 / max(dt1, 1e-3))))
+    ref = RefCpuGemm(N, K, threads, rpt)
+    for _ in range(args.warmup):
+        ref.step()
+    t0 = time.perf_counter()
+    flops = 0.0
+    for _ in range(args.steps):
+        flops += ref.step()
+    dt = time.perf_counter() - t0
+    value = flops / dt / 1e12
+    sample = ("referenceGemmCpp<float> (reference source, compiled -O3 -ffp-contract=off), %d threads x %d rows "
+              "x %d cols of C per step (K=%d) of the %dx%dx%d workload" % (threads, rpt, N, K, M, N, K))
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (fp16 inputs widened)", "data": "synthetic",
+        "config": {"workload": workload, "M_per_rank": M, "N": N, "K": K, "layout": "RC", "threads": threads},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    import kebab_b200 as kb
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
+    M, N, K = args.m, args.n, args.k
+    version = args.version
+    resolved = kb.lib().kebab_resolve_version(version, kb.F16 if args.dtype == "fp16" else kb.BF16, M, N, K)
+    workload = "gemm_rc_%s_%dx%dx%d_msharded" % (args.dtype, M, N, K)
+    stream = torch.cuda.current_stream()
+
+    # Inputs: A shards are generated per rank; B on rank 0, then broadcast.
+    NSETS = 3
+    As, Bs, Cs = [], [], []
+    for s in range(NSETS):
+        A, B = make_inputs(torch, M, N, K, dtype, device, seed=1000 * s + rank)
+        As.append(A)
+        Bs.append(B)
+        Cs.append(torch.empty((N, M), dtype=dtype, device=device))
+    bcast_ms = None
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for s in range(NSETS):
+            dist.broadcast(Bs[s], src=0)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        bcast_ms = e0.elapsed_time(e1) / NSETS
+
+    def step(i):
+        s = i % NSETS
+        rc = kb.gemm_raw(kb.F16 if args.dtype == "fp16" else kb.BF16, As[s].data_ptr(), Bs[s].data_ptr(),
+                         Cs[s].data_ptr(), M, N, K, "RC", version, torch.cuda.current_stream().cuda_stream)
+        if rc != kb.OK:
+            raise kb.KebabError(rc, kb.last_error())
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    rc, code = kb.device_status()
+    if rc != kb.OK:
+        raise RuntimeError("device status 0x%x after warm-up" % code)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev[0].record(stream)
+    for i in range(args.steps):
+        step(i)
+        ev[i + 1].record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    rc, code = kb.device_status()
+    if rc != kb.OK:
+        raise RuntimeError("device status 0x%x after timed steps" % code)
+    total_ms = ev[0].elapsed_time(ev[-1])
+    per_launch = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    flops_rank = 2.0 * M * N * K
+    value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
+
+    # End to end through the public API with host buffers: pinned H2D of this
+    # step's inputs (A shard; B on rank 0 then NCCL broadcast), the GEMM, and
+    # D2H of the C shard, all inside the timed region.
+    hA = As[0].cpu().pin_memory()
+    hB = Bs[0].cpu().pin_memory() if rank == 0 else None
+    hC = torch.empty((N, M), dtype=dtype).pin_memory()
+    dA = torch.empty_like(As[0])
+    dB = torch.empty_like(Bs[0])
+    dC = torch.empty_like(Cs[0])
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        if rank == 0:
+            dB.copy_(hB, non_blocking=True)
+        if world > 1:
+            dist.broadcast(dB, src=0)
+        kb.gemm(dA, dB, dC, version=version)
+        hC.copy_(dC, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = f0.elapsed_time(f1)
+    t = torch.tensor([e2e_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e_value = world * flops_rank * args.e2e_steps / (e2e_ms * 1e-3) / 1e12
+    ok_e2e = bool(torch.isfinite(hC.float()).all().item())
+
+    cublas = None
+    if not args.no_cublas and rank == 0:
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        for _ in range(3):
+            torch.matmul(As[0], Bs[0].t())
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n_cb = 20
+        c0.record(stream)
+        for i in range(n_cb):
+            torch.matmul(As[i % NSETS], Bs[i % NSETS].t())
+        c1.record(stream)
+        torch.cuda.synchronize()
+        cublas = {"value": flops_rank * n_cb / (c0.elapsed_time(c1) * 1e-3) / 1e12, "unit": UNIT,
+                  "what": "torch.matmul (cuBLAS, FP32 accumulate) on the same inputs, 1 GPU"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peaks = load_peaks()
+    avg_launch_ms = float(np.mean(per_launch))
+    achieved = flops_rank / (avg_launch_ms * 1e-3) / 1e12
+    long_loop = total_ms > 1000.0
+    peak = peaks["bf16_tflops_sustained"] if long_loop else peaks["bf16_tflops"]
+    traffic = load_traffic(workload)
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT, "frac": achieved / peak,
+                "traffic": traffic,
+                "peak_kind": "%s %s cuBLAS bf16 GEMM" % (peaks["source"], "sustained" if long_loop else "burst"),
+                "frac_of_nominal_2250": achieved / NOMINAL_DENSE_TFLOPS,
+                "launch_ms_median": float(np.median(per_launch))}
+    out = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": {"workload": workload, "M_per_rank": M, "M_global": M * world, "N": N, "K": K, "layout": "RC",
+                   "version": version, "rung": resolved, "rung_name": kb.version_name(resolved),
+                   "accumulate": "fp32", "inputs": "N(0,1)/sqrt(K), torch generator per rank",
+                   "l2": "3 rotating input sets (%.0f MiB A+B per rank) > 126 MB L2" %
+                         (NSETS * (M * K + N * K) * 2 / 2**20),
+                   "parallelism": "M-sharded x%d, B broadcast once (NCCL)" % world if world > 1 else "1 GPU"},
+        "roofline": roofline,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": (M * K + N * K) * 2,
+                "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps, "finite": ok_e2e},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "broadcast_ms": bcast_ms,
+        "cublas": cublas,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            out["cpu_baseline"] = cpu_baseline_port(M, N, K, args.cpu_seconds)
+        except Exception as e:
+            out["cpu_baseline"] = {"unavailable": str(e)}
+    print(json.dumps(out))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -46,7 +46,28 @@ def run(A_bits, B_bits, M, N, K, dtype, version, device, poison=True):
     return C.float().cpu().numpy().reshape(-1)
 
 
-def assert_close(c_dev, c_ref, what=""):
+# BF16 output: rounding C to BF16 (8-bit significand) alone gives a relative
+# Frobenius error of ~1.1e-3 for ANY implementation, so for BF16 the 1e-3 bar
+# is applied against the oracle rounded to BF16 (what an exact kernel would
+# store), and the raw distance to the FP32 oracle must stay under 4e-3
+# (= 2^-8, one BF16 half-ulp bound). FP16 output is held to 1e-3 directly.
+TOL_REL_FRO_BF16_RAW = 4e-3
+
+
+def round_to(c, dtype):
+    c = np.asarray(c, np.float32)
+    if dtype == O.BF16:
+        u = c.view(np.uint32).astype(np.uint64)
+        u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+        return (u.astype(np.uint32) << 16).view(np.float32)
+    return c.astype(np.float16).astype(np.float32)
+
+
+def assert_close(c_dev, c_ref, what="", dtype=O.F16):
+    if dtype == O.BF16:
+        ok_raw, rel_raw, _ = O.check_tolerance(c_dev, c_ref, TOL_REL_FRO_BF16_RAW, TOL_ELEM)
+        assert ok_raw, "%s: raw rel_fro=%.3e vs FP32 oracle" % (what, rel_raw)
+        c_ref = round_to(c_ref, O.BF16)
     ok, rel, worst = O.check_tolerance(c_dev, c_ref, TOL_REL_FRO, TOL_ELEM)
     assert ok, "%s: rel_fro=%.3e worst_elem_ratio=%.3f nan=%d" % (what, rel, worst, int(np.isnan(c_dev).sum()))
     return rel, worst

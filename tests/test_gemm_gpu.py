@@ -22,7 +22,7 @@ def test_c1_512_uniform(cuda, version, dtype):
     M = N = K = 512
     A, B = inputs(M, N, K, seed=0, dtype=dtype, dist=O.UNIFORM)
     ref = O.gemm(A, B, M, N, K, dtype)
-    assert_close(run(A, B, M, N, K, dtype, version, cuda), ref, "v%d" % version)
+    assert_close(run(A, B, M, N, K, dtype, version, cuda), ref, "v%d" % version, dtype)
 
 
 @pytest.mark.parametrize("version", ALL_RUNGS)
@@ -40,7 +40,7 @@ def test_2048_full(cuda, version, dtype):
     M = N = K = 2048
     A, B = inputs(M, N, K, seed=1, dtype=dtype)
     ref = O.gemm(A, B, M, N, K, dtype)
-    assert_close(run(A, B, M, N, K, dtype, version, cuda), ref, "v%d" % version)
+    assert_close(run(A, B, M, N, K, dtype, version, cuda), ref, "v%d" % version, dtype)
 
 
 @pytest.mark.parametrize("version", [104, 105])
