@@ -1,0 +1,89 @@
+"""The C-ABI library loads and exports every symbol the public headers
+declare, and its host-side validation behaves like the reference operator
+(null pointers / bad dims / float / unknown version rejected) — no GPU."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+import kebab_b200 as kb
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+INC = os.path.join(ROOT, "include")
+
+
+def declared_c_functions():
+    names = set()
+    for d, _, fs in os.walk(INC):
+        for f in fs:
+            if f.endswith(".h"):
+                src = open(os.path.join(d, f)).read()
+                names |= set(re.findall(r"\b(kebab_[a-z0-9_]+)\s*\(", src))
+    return sorted(names)
+
+
+def test_library_loads():
+    assert os.path.exists(kb.LIB_PATH)
+    kb.lib()
+
+
+@pytest.mark.parametrize("name", declared_c_functions())
+def test_c_symbol_exported(name):
+    assert hasattr(kb.lib(), name), name
+
+
+def test_cpp_mirror_symbols_exported():
+    out = subprocess.run(["nm", "-DC", kb.LIB_PATH], capture_output=True, text=True).stdout
+    src = open(os.path.join(INC, "kebab", "cuda", "cuda_gemm.h")).read()
+    rungs = re.findall(r"KEBAB_DECLARE_RUNG\((gemm_\w+)\)", src)
+    assert len(rungs) >= 6
+    for r in rungs:
+        for suf in ("_fp16", "_bf16"):
+            assert "baseline::%s%s(" % (r, suf) in out
+    assert "baseline::gemm(__half const*" in out
+    assert "baseline::gemm(__nv_bfloat16 const*" in out
+    assert "baseline::gemm(float const*" in out
+    assert "baseline::gemm_cuda_version_feature_name(int)" in out
+
+
+def test_null_and_dims_rejected():
+    L = kb.lib()
+    assert L.kebab_gemm(kb.F16, None, None, None, 8, 8, 8, b"RC", 104, None) == kb.EINVAL
+    assert "null pointer" in kb.last_error()
+    p = ctypes.c_void_p(16)
+    assert L.kebab_gemm(kb.F16, p, p, p, 0, 8, 8, b"RC", 104, None) == kb.EINVAL
+    assert "invalid dimensions" in kb.last_error()
+    assert L.kebab_gemm(kb.F16, p, p, p, 8, -1, 8, b"RC", 104, None) == kb.EINVAL
+
+
+def test_float_not_implemented():
+    p = ctypes.c_void_p(16)
+    assert kb.lib().kebab_gemm(kb.F32, p, p, p, 8, 8, 8, b"RC", 104, None) == kb.ENOTSUP
+    assert "not implemented" in kb.last_error()
+
+
+def test_bad_opmode_and_version():
+    p = ctypes.c_void_p(16)
+    assert kb.lib().kebab_gemm(kb.F16, p, p, p, 8, 8, 8, b"XY", 104, None) == kb.EINVAL
+    assert kb.lib().kebab_gemm(kb.F16, p, p, p, 8, 8, 8, b"RC", 999, None) == kb.EINVAL
+    assert "unsupported version" in kb.last_error()
+
+
+def test_version_names_and_mapping():
+    assert kb.version_name(104) == "tma_umma_tmem_warpspecialized_persistent"
+    assert kb.version_name(999) == "unknown"
+    assert kb.version_name(20) == "decomposition_heuristic"
+    for ref_id, rung in kb.REFERENCE_ID_MAP.items():
+        if rung != 120:
+            assert kb.lib().kebab_resolve_version(ref_id, kb.F16, 512, 512, 512) == rung
+    assert set(kb.RUNGS) <= set(kb.list_versions())
+    assert 120 in kb.list_versions()
+
+
+def test_v120_heuristic_without_gpu():
+    # Falls back to 148 SMs when no device can be queried.
+    r_big = kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192)
+    r_small = kb.lib().kebab_resolve_version(120, kb.F16, 256, 256, 8192)
+    assert r_big == 105 and r_small == 104
