@@ -20,7 +20,7 @@ const char* gemm_cuda_version_feature_name(int version);
 
 // Replace the three overloads at kebab/lib/cuda/cuda_gemm.cu:112, :246, :259.
 // A: M x K, B: K x N, C: M x N column-major; opmode "RC" (A row-major, B
-// column-major). version: a B200 rung (1, 101..105, 120) or a reference id.
+// column-major). version: a B200 rung (1, 101..106, 120) or a reference id.
 void gemm(const float* A, const float* B, float* C, int M, int N, int K, const char* opmode = "RC",
           int version = 1, cudaStream_t stream = 0);
 void gemm(const __half* A, const __half* B, __half* C, int M, int N, int K, const char* opmode = "RC",
@@ -41,6 +41,7 @@ KEBAB_DECLARE_RUNG(gemm_v102_tma_umma_tmem)                                   //
 KEBAB_DECLARE_RUNG(gemm_v103_tma_umma_tmem_warpspecialized)                   // + producer/MMA/epilogue warps
 KEBAB_DECLARE_RUNG(gemm_v104_tma_umma_tmem_warpspecialized_persistent)        // + persistent scheduler
 KEBAB_DECLARE_RUNG(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta)   // + cta_group::2 pairs
+KEBAB_DECLARE_RUNG(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny)      // M <= 256: swap-AB, cluster split-K
 #undef KEBAB_DECLARE_RUNG
 
 }  // namespace baseline

@@ -47,7 +47,7 @@ typedef enum kebab_dtype {
  *   const char* opmode, int version, cudaStream_t stream)
  *   (kebab/lib/cuda/cuda_gemm.cu:112 for __half, :259 for __nv_bfloat16,
  *   :246 for float), returning a status instead of printing and returning.
- * `version` is one of the B200 rungs (1, 101..105, 120) or a reference
+ * `version` is one of the B200 rungs (1, 101..106, 120) or a reference
  * version id (2..20, 41), which maps to the B200 rung with the same idea
  * (kebab_version_name() tells which). opmode NULL means "RC". */
 int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,

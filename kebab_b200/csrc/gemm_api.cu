@@ -36,6 +36,7 @@ const Rung kRungs[] = {
     {103, "tma_umma_tmem_warpspecialized", launch_v103_ws},
     {104, "tma_umma_tmem_warpspecialized_persistent", launch_v104_persistent},
     {105, "tma_umma_tmem_warpspecialized_persistent_2cta", launch_v105_pair},
+    {106, "tma_umma_tmem_swapab_splitk_cluster_skinny", launch_v106_skinny},
 };
 
 const Rung* find_rung(int id) {
@@ -69,7 +70,11 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count) {
     if (m == "DP" || m == "DATAPARALLEL") return 103;
     if (m == "PERSISTENT") return 104;
     if (m == "PAIR" || m == "2CTA") return 105;
+    if (m == "SKINNY" || m == "SPLITK") return 106;
   }
+  // Decode-like shapes: too few 128-row tiles to occupy the GPU; stream B
+  // with the swap-AB split-K rung.
+  if (M <= 256) return 106;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
   if (pair_tiles >= sm_count / 2) return 105;
@@ -181,6 +186,7 @@ KEBAB_RUNG_LAUNCHER(gemm_v102_tma_umma_tmem, 102)
 KEBAB_RUNG_LAUNCHER(gemm_v103_tma_umma_tmem_warpspecialized, 103)
 KEBAB_RUNG_LAUNCHER(gemm_v104_tma_umma_tmem_warpspecialized_persistent, 104)
 KEBAB_RUNG_LAUNCHER(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta, 105)
+KEBAB_RUNG_LAUNCHER(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny, 106)
 #undef KEBAB_RUNG_LAUNCHER
 
 }  // namespace baseline

@@ -53,6 +53,8 @@ int launch_v102_umma(const GemmProblem& p);
 int launch_v103_ws(const GemmProblem& p);
 int launch_v104_persistent(const GemmProblem& p);
 int launch_v105_pair(const GemmProblem& p);
+int launch_v106_skinny(const GemmProblem& p);
+int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and
 // row pitches (K % 8 == 0 for A/B rows, M % 8 == 0 for C columns).

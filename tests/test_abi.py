@@ -85,5 +85,6 @@ def test_version_names_and_mapping():
 def test_v120_heuristic_without_gpu():
     # Falls back to 148 SMs when no device can be queried.
     r_big = kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192)
-    r_small = kb.lib().kebab_resolve_version(120, kb.F16, 256, 256, 8192)
-    assert r_big == 105 and r_small == 104
+    r_small = kb.lib().kebab_resolve_version(120, kb.F16, 1024, 256, 8192)
+    r_skinny = kb.lib().kebab_resolve_version(120, kb.F16, 64, 8192, 8192)
+    assert r_big == 105 and r_small == 104 and r_skinny == 106
