@@ -1,0 +1,71 @@
+"""M-sharded GEMM over NCCL on 2+ GPUs (skipped with fewer): each rank runs
+kebab_gemm on its row block after B is broadcast once; the gathered C must
+equal the single-GPU result bit for bit (same rung, same per-element K
+order). Child processes, NVLS off, every rank finishes its kernels before
+any collective."""
+import os
+import socket
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CHILD = r'''
+import os, sys, torch, torch.distributed as dist
+sys.path.insert(0, os.environ["KB_ROOT"])
+import kebab_b200 as kb
+from kebab_b200.shard import row_block, shard_a, broadcast_b, sharded_gemm, gather_c
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dev = torch.device("cuda", rank)
+dist.init_process_group("nccl", device_id=dev)
+M, N, K = 2048 * world, 1536, 1024
+g = torch.Generator(device=dev).manual_seed(7)
+A = (torch.randn(M, K, generator=g, device=dev) / K ** 0.5).half()
+B = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).half()
+if rank != 0:
+    B.zero_()
+broadcast_b(B, src=0)
+blk = row_block(M, world, rank)
+C = sharded_gemm(shard_a(A, blk).contiguous(), B, version=int(os.environ["KB_VERSION"]))
+torch.cuda.synchronize()
+assert kb.device_status()[0] == kb.OK
+Cg = gather_c(C, world)
+if rank == 0:
+    full = kb.gemm(A, B, version=int(os.environ["KB_VERSION"]))
+    torch.cuda.synchronize()
+    same = torch.equal(full.view(torch.int16), Cg.view(torch.int16))
+    print("RESULT", "bitexact" if same else "mismatch", flush=True)
+dist.barrier()
+dist.destroy_process_group()
+'''
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("version", [104, 105])
+def test_sharded_bitexact(cuda, version):
+    import torch
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs 2+ GPUs")
+    port = _port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), KB_ROOT=ROOT, KB_VERSION=str(version), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", CHILD], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = [p.communicate(timeout=300)[0] for p in procs]
+    assert all(p.returncode == 0 for p in procs), "\n".join(o[-2000:] for o in outs)
+    assert "RESULT bitexact" in outs[0], outs[0][-2000:]
