@@ -152,3 +152,102 @@ def set_wait_timeout_us(us):
 
 def probe_wait_timeout(timeout_us=1000, stream=None):
     return lib().kebab_probe_wait_timeout(_stream_ptr(stream), timeout_us)
+
+
+# ----------------------------------------------------------------------------- 2:4 sparsity
+def _sp():
+    L = lib()
+    if not getattr(L, "_sp_typed", False):
+        c = ctypes
+        for name, args in {
+            "kebab_sparse24_prune": [c.c_int, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p],
+            "kebab_sparse24_pack": [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p],
+            "kebab_sparse24_group_codes": [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p],
+            "kebab_sparse24_meta_cutlass": [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p],
+            "kebab_sparse24_meta_ordered": [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_int, c.c_void_p],
+            "kebab_sparse24_compress": [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64,
+                                        c.c_void_p],
+            "kebab_gemm_sparse24": [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64,
+                                    c.c_int64, c.c_void_p],
+        }.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = c.c_int
+        L.kebab_sparse24_e_bytes.argtypes = [c.c_int64, c.c_int64]
+        L.kebab_sparse24_e_bytes.restype = c.c_int64
+        L._sp_typed = True
+    return L
+
+
+def sparse24_prune(A, out=None, stream=None):
+    import torch
+    M, K = A.shape
+    out = torch.empty_like(A) if out is None else out
+    check(_sp().kebab_sparse24_prune(_dtype_code(A), A.data_ptr(), out.data_ptr(), M, K, _stream_ptr(stream)))
+    return out
+
+
+def sparse24_pack(A_pruned, stream=None):
+    """-> (A_packed [M, K/2], meta [M, K/2] int32 positions). Raises
+    KebabError(ESPARSE) if a group does not hold exactly two non-zeros."""
+    import torch
+    M, K = A_pruned.shape
+    packed = torch.empty((M, K // 2), dtype=A_pruned.dtype, device=A_pruned.device)
+    meta = torch.empty((M, K // 2), dtype=torch.int32, device=A_pruned.device)
+    check(_sp().kebab_sparse24_pack(_dtype_code(A_pruned), A_pruned.data_ptr(), packed.data_ptr(), meta.data_ptr(),
+                                    M, K, _stream_ptr(stream)))
+    return packed, meta
+
+
+def sparse24_group_codes(meta, K, stream=None):
+    import torch
+    M = meta.shape[0]
+    codes = torch.empty((M, K // 4), dtype=torch.int32, device=meta.device)
+    check(_sp().kebab_sparse24_group_codes(meta.data_ptr(), codes.data_ptr(), M, K, _stream_ptr(stream)))
+    return codes
+
+
+def sparse24_meta_cutlass(meta, K, stream=None):
+    import torch
+    M = meta.shape[0]
+    out = torch.empty(((M // 16) * (K // 32) * 64,), dtype=torch.int32, device=meta.device)
+    check(_sp().kebab_sparse24_meta_cutlass(meta.data_ptr(), out.data_ptr(), M, K, _stream_ptr(stream)))
+    return out
+
+
+def sparse24_meta_ordered(codes, K, rowpair, stream=None):
+    import torch
+    M = codes.shape[0]
+    out = torch.empty(((M // 16) * (K // 32) * 32,), dtype=torch.int32, device=codes.device)
+    check(_sp().kebab_sparse24_meta_ordered(codes.data_ptr(), out.data_ptr(), M, K, 1 if rowpair else 0,
+                                            _stream_ptr(stream)))
+    return out
+
+
+def sparse24_compress(A_pruned, stream=None):
+    """-> (A_packed [M, K/2], E uint8 buffer) operands of gemm_sparse24."""
+    import torch
+    M, K = A_pruned.shape
+    nbytes = _sp().kebab_sparse24_e_bytes(M, K)
+    if nbytes < 0:
+        raise KebabError(-nbytes, "2:4 compress needs M % 128 == 0 and K % 128 == 0")
+    packed = torch.empty((M, K // 2), dtype=A_pruned.dtype, device=A_pruned.device)
+    E = torch.empty((nbytes,), dtype=torch.uint8, device=A_pruned.device)
+    check(_sp().kebab_sparse24_compress(_dtype_code(A_pruned), A_pruned.data_ptr(), packed.data_ptr(), E.data_ptr(),
+                                        M, K, _stream_ptr(stream)))
+    return packed, E
+
+
+def gemm_sparse24(A_packed, E, B, C=None, stream=None):
+    """C = A * B with A 2:4 sparse (A_packed [M, K/2], E from sparse24_compress),
+    B [N, K] (column-major K x N); C [N, M] column-major."""
+    import torch
+    M, Kh = A_packed.shape
+    N, K = B.shape
+    if K != 2 * Kh:
+        raise KebabError(EINVAL, "A_packed must be [M, K/2]")
+    if C is None:
+        C = torch.empty((N, M), dtype=B.dtype, device=B.device)
+    check(_sp().kebab_gemm_sparse24(_dtype_code(B), A_packed.data_ptr(), E.data_ptr(), B.data_ptr(), C.data_ptr(),
+                                    M, N, K, _stream_ptr(stream)))
+    return C

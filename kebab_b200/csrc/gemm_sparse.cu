@@ -1,0 +1,366 @@
+// 2:4 structured-sparse GEMM on tcgen05.mma.sp (kind::f16), FP32 accumulate.
+//
+// C (M x N, column-major) = A (M x K, 2:4 sparse, given compressed as
+// A_packed M x K/2 + metadata E) * B (K x N, column-major). Same warp roles,
+// ring and epilogue as the dense persistent kernel (gemm_umma.cuh); per
+// 128-wide logical K block a stage holds
+//   A_packed 128 x 64 (16 KB, 128-byte swizzle),
+//   B        128 x 128 as two 64-wide swizzled sub-tiles (32 KB),
+//   E        128 rows x 16 bytes (2 KB): the metadata of the 128 x 128 block,
+//            already in the order tcgen05.cp.128x128b expects (see
+//            sparse24.cu:compress_kernel);
+// the MMA lane copies E to 4 TMEM columns (tcgen05.cp) and issues four
+// 128 x BN x 32 sparse MMAs, MMA j reading metadata column j.
+//   CG=1: 128 x 128 tiles, two accumulators (epilogue overlaps the next tile).
+//   CG=2: CTA pairs, 256 x 256 tiles (cta_group::2): B traffic per CTA is the
+//         same as CG=1 while each MMA does twice the work; one accumulator
+//         (2 x 256 columns would leave no room for the metadata).
+// The reference has no sparse GEMM (its 2:4 path is one mma.sp tile,
+// kebab/lib/microbench/sparse_mma.cu:347-428).
+#include <algorithm>
+#include <mutex>
+
+#include "gemm_umma.cuh"
+#include "internal.h"
+#include "kebab/sparse24.h"
+
+namespace kb {
+
+namespace {
+
+template <int STAGES>
+struct SparseSmem {
+  static constexpr int A_STAGE = 128 * 64 * 2;
+  static constexpr int B_SUB = 128 * 64 * 2;
+  static constexpr int B_STAGE = 2 * B_SUB;
+  static constexpr int E_STAGE = 2048;
+  static constexpr int C_SUB = 32 * 32 * 2;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
+  static constexpr int OFF_E = OFF_B + STAGES * B_STAGE;
+  static constexpr int OFF_C = OFF_E + STAGES * E_STAGE;
+  static constexpr int OFF_BAR = OFF_C + 4 * 2 * C_SUB;
+  static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
+  static constexpr int BYTES = OFF_BAR + NUM_BARS * 8 + 16;
+  static constexpr int ALLOC = BYTES + 1024;
+  static_assert(ALLOC <= 232448, "shared memory budget exceeded");
+};
+
+template <typename T, int CG, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    gemm_sparse_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmC,
+                       const UmmaArgs args) {
+  using L = SparseSmem<STAGES>;
+  constexpr int BN = 128 * CG;
+  constexpr int BM_T = 128 * CG;
+  constexpr int ACCS = (2 * BN + 4 * STAGES <= 512) ? 2 : 1;
+  constexpr int E_COL0 = ACCS * BN;
+  constexpr int TMEM_COLS = 512;
+  static_assert(E_COL0 + 4 * STAGES <= TMEM_COLS, "metadata columns must fit in TMEM");
+  constexpr uint32_t IDESC = umma_idesc_f16_sparse(BM_T, BN, ElemTraits<T>::kBf16);
+  constexpr uint32_t TX_BYTES = (L::A_STAGE + L::B_STAGE + L::E_STAGE) * CG;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tmem_full = bars + 2 * STAGES;
+  uint64_t* tmem_empty = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + L::NUM_BARS);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
+  const bool leader = (rank == 0);
+  const WaitCtx& ctx = args.ctx;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmE);
+    tma_prefetch_desc(&tmC);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 4 * CG);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc<CG>(tmem_slot, TMEM_COLS);
+    tmem_relinquish<CG>();
+  }
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int cluster_id = blockIdx.x / CG;
+  const int num_clusters = gridDim.x / CG;
+  const int num_kb = args.K / 128;  // K % 128 == 0 (checked on the host)
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      const uint32_t full_leader0 = (CG == 2) ? mapa_shared(smem_u32(&full[0]), 0) : 0u;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        int mb, nb;
+        tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+        const int m0 = mb * BM_T + (int)rank * 128;
+        const int n0 = nb * BN + (int)rank * 128;
+        const int e_row0 = (m0 / 128) * num_kb * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, ctx, SITE_EMPTY)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sA = smem + L::OFF_A + stage * L::A_STAGE;
+          uint8_t* sB = smem + L::OFF_B + stage * L::B_STAGE;
+          uint8_t* sE = smem + L::OFF_E + stage * L::E_STAGE;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+            tma_load_2d(sA, &tmA, &full[stage], kb * 64, m0);
+            tma_load_2d(sB, &tmB, &full[stage], kb * 128, n0);
+            tma_load_2d(sB + L::B_SUB, &tmB, &full[stage], kb * 128 + 64, n0);
+            tma_load_2d(sE, &tmE, &full[stage], 0, e_row0 + kb * 128);
+          } else {
+            if (leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+            const uint32_t fb = full_leader0 + stage * 8u;
+            tma_load_2d_pair(sA, &tmA, fb, kb * 64, m0);
+            tma_load_2d_pair(sB, &tmB, fb, kb * 128, n0);
+            tma_load_2d_pair(sB + L::B_SUB, &tmB, fb, kb * 128 + 64, n0);
+            tma_load_2d_pair(sE, &tmE, fb, 0, e_row0 + kb * 128);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, any = false;
+      for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
+          const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
+          const uint32_t e_addr = smem_u32(smem + L::OFF_E + stage * L::E_STAGE);
+          const uint32_t e_tmem = tmem_base + (uint32_t)(E_COL0 + stage * 4);
+          // 128 rows x 16 bytes, 8-row core matrices 128 bytes apart, no swizzle.
+          tmem_cp_128x128b<CG>(e_tmem, umma_desc(e_addr, 16, 128, 0));
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint64_t ad = umma_desc_sw128(a_addr + j * 32);
+            const uint64_t bd = umma_desc_sw128(b_addr + (j >> 1) * L::B_SUB + (j & 1) * 64);
+            umma_f16_sp<CG>(d_tmem, ad, bd, e_tmem + j, IDESC, (kb | j) != 0 ? 1u : 0u);
+          }
+          any = true;
+          if constexpr (CG == 1) umma_commit_cg1(&empty[stage]);
+          else umma_commit_cg2_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        if constexpr (CG == 1) umma_commit_cg1(&tmem_full[acc]);
+        else umma_commit_cg2_mc(&tmem_full[acc], 0x3);
+        if (++acc == ACCS) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok && any) {
+        if constexpr (CG == 1) umma_commit_cg1(drain);
+        else umma_commit_cg2_mc(drain, 0x1);
+        WaitCtx d{ctx.status, 50000000ull};
+        mbar_wait(drain, 0, d, SITE_DRAIN);
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int ew = warp - 2;
+    T* stage_c = reinterpret_cast<T*>(smem + L::OFF_C + ew * 2 * L::C_SUB);
+    const uint32_t tmem_empty_leader0 = (CG == 2) ? mapa_shared(smem_u32(&tmem_empty[0]), 0) : 0u;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sub = 0;
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+      int mb, nb;
+      tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+      const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
+      const int n0 = nb * BN;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), v);
+        tmem_ld_wait();
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (CG == 1) mbar_arrive(&tmem_empty[acc]);
+            else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
+          }
+        }
+        T* buf = stage_c + (sub & 1) * (32 * 32);
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
+          tma_store_commit();
+        }
+        ++sub;
+      }
+      if (++acc == ACCS) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  if constexpr (CG == 2) cluster_sync(); else __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc<CG>(tmem_base, TMEM_COLS);
+  }
+}
+
+// E viewed as a 2-D array of uint16: 8 per 16-byte row, 128 rows per block.
+int make_tmap_e(CUtensorMap* out, const void* E, int64_t M, int64_t K) {
+  const uint64_t rows = (uint64_t)(M / 128) * (uint64_t)(K / 128) * 128;
+  return make_tmap_2d(out, E, KEBAB_F16, rows, 8, 8, 128, 8, false);
+}
+
+template <typename T, int CG, int STAGES>
+int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                  cudaStream_t stream) {
+  using L = SparseSmem<STAGES>;
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  UmmaArgs args;
+  if ((rc = wait_ctx(&args.ctx))) return rc;
+  CUtensorMap tA, tB, tE, tC;
+  if ((rc = make_tmap_2d(&tA, Ap, dtype, M, K / 2, K / 2, 128, 64, true))) return rc;
+  if ((rc = make_tmap_2d(&tB, B, dtype, N, K, K, 128, 64, true))) return rc;
+  if ((rc = make_tmap_e(&tE, E, M, K))) return rc;
+  if ((rc = make_tmap_2d(&tC, C, dtype, N, M, M, 32, 32, false))) return rc;
+  constexpr int BM_T = 128 * CG, BN = 128 * CG;
+  args.M = (int)M;
+  args.N = (int)N;
+  args.K = (int)K;
+  args.tiles_m = (int)((M + BM_T - 1) / BM_T);
+  args.tiles_n = (int)((N + BN - 1) / BN);
+  args.group_m = 16;
+  const long long tiles = (long long)args.tiles_m * args.tiles_n;
+  auto kern = gemm_sparse_kernel<T, CG, STAGES>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  const int di = dev->device & 63;
+  std::call_once(once[di], [&] {
+    attr_err[di] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  });
+  if (attr_err[di] != cudaSuccess) return cuda_fail(attr_err[di], "cudaFuncSetAttribute");
+  int max_clusters = dev->sm_count / CG;
+  if (CG > 1) {
+    static int max_active[64] = {0};
+    if (max_active[di] == 0) {
+      cudaLaunchConfig_t qc = {};
+      qc.gridDim = dim3(CG * max_clusters, 1, 1);
+      qc.blockDim = dim3(192, 1, 1);
+      qc.dynamicSmemBytes = L::ALLOC;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = CG;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      qc.attrs = qa;
+      qc.numAttrs = 1;
+      int n = 0;
+      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
+      max_active[di] = (e == cudaSuccess && n > 0) ? n : max_clusters;
+      (void)cudaGetLastError();
+    }
+    max_clusters = std::min(max_clusters, max_active[di]);
+  }
+  const int clusters = (int)std::min<long long>(tiles, max_clusters);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CG * clusters, 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = L::ALLOC;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CG;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tE, tC, args);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_sparse launch");
+  return KEBAB_OK;
+}
+
+}  // namespace
+}  // namespace kb
+
+using namespace kb;
+
+extern "C" int kebab_gemm_sparse24(kebab_dtype dtype, const void* A_packed, const void* E, const void* B, void* C,
+                                   int64_t M, int64_t N, int64_t K, kebab_stream_t stream) {
+  if (!A_packed || !E || !B || !C) return fail(KEBAB_EINVAL, "null pointer passed to kebab_gemm_sparse24");
+  if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "2:4 GEMM supports F16 and BF16");
+  if (M <= 0 || N <= 0 || K <= 0 || M % 128 || K % 128)
+    return fail(KEBAB_EINVAL, "2:4 GEMM needs M % 128 == 0 and K % 128 == 0 (N > 0)");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return fail(KEBAB_EINVAL, "sizes must fit in int32");
+  if ((reinterpret_cast<uintptr_t>(A_packed) | reinterpret_cast<uintptr_t>(E) | reinterpret_cast<uintptr_t>(B) |
+       reinterpret_cast<uintptr_t>(C)) & 15u)
+    return fail(KEBAB_EINVAL, "2:4 GEMM buffers must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  // KEBAB_SPARSE_CG=1 forces 128 x 128 single-CTA tiles (default: CTA pairs).
+  const char* env = std::getenv("KEBAB_SPARSE_CG");
+  const bool one = env && env[0] == '1';
+  if (dtype == KEBAB_F16)
+    return one ? launch_sparse<__half, 1, 4>(dtype, A_packed, E, B, C, M, N, K, s)
+               : launch_sparse<__half, 2, 4>(dtype, A_packed, E, B, C, M, N, K, s);
+  return one ? launch_sparse<__nv_bfloat16, 1, 4>(dtype, A_packed, E, B, C, M, N, K, s)
+             : launch_sparse<__nv_bfloat16, 2, 4>(dtype, A_packed, E, B, C, M, N, K, s);
+}

@@ -244,6 +244,14 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// General shared-memory matrix descriptor: `layout` 0 = no swizzle,
+// 2 = 128-byte swizzle; byte offsets are multiples of 16.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo, uint32_t layout) {
+  return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16 |
+         static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32 | static_cast<uint64_t>(1u) << 46 |
+         static_cast<uint64_t>(layout & 7u) << 61;
+}
+
 // Instruction descriptor for kind::f16 with FP32 accumulation, both operands
 // K-major. `ab_bf16` selects BF16 (1) or FP16 (0) for A and B.
 __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int ab_bf16) {
@@ -252,6 +260,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, int ab_bf16)
          | (static_cast<uint32_t>(ab_bf16) << 10)      // B format
          | (static_cast<uint32_t>(N >> 3) << 17)       // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);      // M / 16
+}
+
+// Sparse variant (2:4 A): bit 2 = sparse; the metadata selector (bits 0..1) is 0.
+__host__ __device__ constexpr uint32_t umma_idesc_f16_sparse(int M, int N, int ab_bf16) {
+  return umma_idesc_f16(M, N, ab_bf16) | (1u << 2);
 }
 
 __device__ __forceinline__ void umma_f16_cg1(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
@@ -272,6 +285,36 @@ __device__ __forceinline__ void umma_f16_cg2(uint32_t d_tmem, uint64_t a_desc, u
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
+}
+
+// 2:4 sparse A: logical K = 32 per instruction; metadata at TMEM `e_tmem`.
+template <int CG>
+__device__ __forceinline__ void umma_f16_sp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t e_tmem,
+                                            uint32_t idesc, uint32_t accumulate) {
+  if constexpr (CG == 1)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::1.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %5, 0;\n\t"
+        "tcgen05.mma.sp.cta_group::2.kind::f16 [%0], %1, %2, [%3], %4, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Shared memory -> TMEM copy of 128 rows x 128 bits (4 columns), source
+// described by a matrix descriptor.
+template <int CG>
+__device__ __forceinline__ void tmem_cp_128x128b(uint32_t taddr, uint64_t sdesc) {
+  if constexpr (CG == 1)
+    asm volatile("tcgen05.cp.cta_group::1.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+  else
+    asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
 // Signal `bar` (this CTA) once all tcgen05 ops issued so far by this thread complete.
