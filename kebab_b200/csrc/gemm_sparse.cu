@@ -10,7 +10,8 @@
 //            already in the order tcgen05.cp.128x128b expects (see
 //            sparse24.cu:compress_kernel);
 // the MMA lane copies E to 4 TMEM columns (tcgen05.cp) and issues four
-// 128 x BN x 32 sparse MMAs, MMA j reading metadata column j.
+// 128 x BN x 32 sparse MMAs, MMA j reading metadata column j (addressed as
+// the even column 2*(j/2) plus selector j%2 in the instruction descriptor).
 //   CG=1: 128 x 128 tiles, two accumulators (epilogue overlaps the next tile).
 //   CG=2: CTA pairs, 256 x 256 tiles (cta_group::2): B traffic per CTA is the
 //         same as CG=1 while each MMA does twice the work; one accumulator
@@ -178,7 +179,10 @@ __global__ void __launch_bounds__(192, 1)
           for (int j = 0; j < 4; ++j) {
             const uint64_t ad = umma_desc_sw128(a_addr + j * 32);
             const uint64_t bd = umma_desc_sw128(b_addr + (j >> 1) * L::B_SUB + (j & 1) * 64);
-            umma_f16_sp<CG>(d_tmem, ad, bd, e_tmem + j, IDESC, (kb | j) != 0 ? 1u : 0u);
+            // The metadata address must be 2-column aligned; the odd column of
+            // a pair is chosen with the descriptor's selector (bits 0..1).
+            umma_f16_sp<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)(j & ~1), IDESC | (uint32_t)(j & 1),
+                            (kb | j) != 0 ? 1u : 0u);
           }
           any = true;
           if constexpr (CG == 1) umma_commit_cg1(&empty[stage]);
