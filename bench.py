@@ -46,6 +46,8 @@ def parse():
     p.add_argument("--n", type=int, default=8192)
     p.add_argument("--k", type=int, default=8192)
     p.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
+    p.add_argument("--workload", default="dense", choices=["dense", "sparse24"],
+                   help="dense GEMM (BASELINE config 2) or 2:4 sparse GEMM (config 5)")
     p.add_argument("--e2e-steps", type=int, default=5)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
@@ -258,7 +260,8 @@ def main():
     M, N, K = args.m, args.n, args.k
     version = args.version
     resolved = kb.lib().kebab_resolve_version(version, kb.F16 if args.dtype == "fp16" else kb.BF16, M, N, K)
-    workload = "gemm_rc_%s_%dx%dx%d_msharded" % (args.dtype, M, N, K)
+    sparse = args.workload == "sparse24"
+    workload = "%s_rc_%s_%dx%dx%d_msharded" % ("gemm_sparse24" if sparse else "gemm", args.dtype, M, N, K)
     stream = torch.cuda.current_stream()
 
     # Inputs: A shards are generated per rank; B on rank 0, then broadcast.
@@ -281,8 +284,38 @@ def main():
         torch.cuda.synchronize()
         bcast_ms = e0.elapsed_time(e1) / NSETS
 
+    packer = None
+    if sparse:
+        # Config 5: A dense N(0,1) pruned 2:4 and compressed once, outside timing;
+        # the prune and compress kernels are timed separately (GB/s).
+        Ps, Es = [], []
+        for s in range(NSETS):
+            As[s] = As[s] * float(np.sqrt(K))  # N(0,1) activations, as config 5 asks
+            t0, t1, t2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            t0.record(stream)
+            pr = kb.sparse24_prune(As[s])
+            t1.record(stream)
+            pk, E = kb.sparse24_compress(pr)
+            t2.record(stream)
+            torch.cuda.synchronize()
+            if s == NSETS - 1:
+                mk = M * K
+                packer = {"prune_gbs": 4.0 * mk / (t0.elapsed_time(t1) * 1e-3) / 1e9,
+                          "compress_gbs": (2.0 * mk + mk + mk / 8.0) / (t1.elapsed_time(t2) * 1e-3) / 1e9,
+                          "prune_ms": t0.elapsed_time(t1), "compress_ms": t1.elapsed_time(t2)}
+            Ps.append(pk)
+            Es.append(E)
+            As[s] = pr
+
     def step(i):
         s = i % NSETS
+        if sparse:
+            rc = kb._sp().kebab_gemm_sparse24(kb.F16 if args.dtype == "fp16" else kb.BF16, Ps[s].data_ptr(),
+                                             Es[s].data_ptr(), Bs[s].data_ptr(), Cs[s].data_ptr(), M, N, K,
+                                             torch.cuda.current_stream().cuda_stream)
+            if rc != kb.OK:
+                raise kb.KebabError(rc, kb.last_error())
+            return
         rc = kb.gemm_raw(kb.F16 if args.dtype == "fp16" else kb.BF16, As[s].data_ptr(), Bs[s].data_ptr(),
                          Cs[s].data_ptr(), M, N, K, "RC", version, torch.cuda.current_stream().cuda_stream)
         if rc != kb.OK:
@@ -332,13 +365,24 @@ def main():
     dB = torch.empty_like(Bs[0])
     dC = torch.empty_like(Cs[0])
 
+    if sparse:
+        hA = Ps[0].cpu().pin_memory()
+        hE = Es[0].cpu().pin_memory()
+        dA = torch.empty_like(Ps[0])
+        dE = torch.empty_like(Es[0])
+
     def e2e_step():
         dA.copy_(hA, non_blocking=True)
+        if sparse:
+            dE.copy_(hE, non_blocking=True)
         if rank == 0:
             dB.copy_(hB, non_blocking=True)
         if world > 1:
             dist.broadcast(dB, src=0)
-        kb.gemm(dA, dB, dC, version=version)
+        if sparse:
+            kb.gemm_sparse24(dA, dE, dB, dC)
+        else:
+            kb.gemm(dA, dB, dC, version=version)
         hC.copy_(dC, non_blocking=True)
 
     e2e_step()
@@ -358,6 +402,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     e2e_ms = float(t.item())
     e2e_value = world * flops_rank * args.e2e_steps / (e2e_ms * 1e-3) / 1e12
+    h2d = (M * K + N * K) * 2 if not sparse else M * K + N * K * 2 + M * K // 8
     ok_e2e = bool(torch.isfinite(hC.float()).all().item())
 
     cublas = None
@@ -368,14 +413,14 @@ def main():
             torch.matmul(As[0], Bs[0].t())
         torch.cuda.synchronize()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        n_cb = 20
+        n_cb = args.steps  # same loop length as the timed region (same power state)
         c0.record(stream)
         for i in range(n_cb):
             torch.matmul(As[i % NSETS], Bs[i % NSETS].t())
         c1.record(stream)
         torch.cuda.synchronize()
         cublas = {"value": flops_rank * n_cb / (c0.elapsed_time(c1) * 1e-3) / 1e12, "unit": UNIT,
-                  "what": "torch.matmul (cuBLAS, FP32 accumulate) on the same inputs, 1 GPU"}
+                  "what": "torch.matmul (cuBLAS, FP32 accumulate) on the same inputs, 1 GPU, same number of back-to-back launches"}
 
     if rank != 0:
         if world > 1:
@@ -388,11 +433,22 @@ def main():
     long_loop = total_ms > 1000.0
     peak = peaks["bf16_tflops_sustained"] if long_loop else peaks["bf16_tflops"]
     traffic = load_traffic(workload)
+    peak_kind = "%s %s cuBLAS bf16 GEMM" % (peaks["source"], "sustained" if long_loop else "burst")
+    if sparse:
+        peak *= 2.0  # 2:4 sparse tensor-core peak = 2 x dense, dense-equivalent FLOPs
+        peak_kind = "2 x " + peak_kind + " (2:4 sparse rate)"
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": UNIT, "frac": achieved / peak,
-                "traffic": traffic,
-                "peak_kind": "%s %s cuBLAS bf16 GEMM" % (peaks["source"], "sustained" if long_loop else "burst"),
-                "frac_of_nominal_2250": achieved / NOMINAL_DENSE_TFLOPS,
+                "traffic": traffic, "peak_kind": peak_kind,
+                "frac_of_nominal_2250": achieved / NOMINAL_DENSE_TFLOPS * (0.5 if sparse else 1.0),
                 "launch_ms_median": float(np.median(per_launch))}
+    if resolved == 106 and not sparse:
+        # Decode-shaped GEMM: HBM-bound; report bytes against measured HBM copy bandwidth.
+        nbytes = 2.0 * (M * K + N * K + M * N)
+        gbs = nbytes / (avg_launch_ms * 1e-3) / 1e9
+        roofline = {"bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                    "frac": gbs / peaks["hbm_gbs"], "traffic": traffic, "algorithmic_bytes": nbytes,
+                    "peak_kind": "%s HBM copy" % peaks["source"], "tflops": achieved,
+                    "launch_ms_median": float(np.median(per_launch))}
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
@@ -404,13 +460,17 @@ def main():
                          (NSETS * (M * K + N * K) * 2 / 2**20),
                    "parallelism": "M-sharded x%d, B broadcast once (NCCL)" % world if world > 1 else "1 GPU"},
         "roofline": roofline,
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": (M * K + N * K) * 2,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": M * N * 2, "steps": args.e2e_steps, "finite": ok_e2e},
         "gpu_launches": args.steps,
         "clocks": clocks,
         "broadcast_ms": bcast_ms,
         "cublas": cublas,
     }
+    if sparse:
+        out["metric"] = "2:4 sparse FP16 RC GEMM TFLOP/s (dense-equivalent 2MNK) @ M=N=K=8192"
+        out["useful_tflops"] = value / 2.0
+        out["packer"] = packer
     if world == 1 and not args.no_cpu_baseline:
         try:
             out["cpu_baseline"] = cpu_baseline_port(M, N, K, args.cpu_seconds)

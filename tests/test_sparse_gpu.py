@@ -119,3 +119,82 @@ def test_gemm_sparse24(cuda, cg, shape, monkeypatch):
 @pytest.mark.parametrize("cg", [1, 2])
 def test_gemm_sparse24_bf16(cuda, cg, monkeypatch):
     _sparse_case(cuda, 512, 512, 1024, O.BF16, cg, monkeypatch, seed=2)
+
+
+def _host_e(meta, M, K, mode, lanes):
+    """Metadata buffer assembled on the host under a layout hypothesis."""
+    E = np.zeros((M // 128) * (K // 128) * 2048, np.uint8)
+    for m in range(M):
+        for kc in range(K // 16):
+            bits = 0
+            for g in range(4):
+                gi = kc * 4 + g
+                p0, p1 = int(meta[m * (K // 2) + 2 * gi]), int(meta[m * (K // 2) + 2 * gi + 1])
+                nib = {"p0|p1<<2": p0 | (p1 << 2), "p1|p0<<2": p1 | (p0 << 2),
+                       "code": int(O.lib().kbo_encode_2of4(p0, p1))}[mode]
+                bits |= nib << (4 * g)
+            k = kc * 16
+            tile = (m // 128) * (K // 128) + k // 128
+            mi, ki = m % 128, k % 128
+            if lanes == "pair-rows":  # lane = m0 + 8 k1 + 16 m2, rows r / r+8 in the low / high halves
+                byte = 16 * (mi & 7) + 2 * ((mi >> 3) & 1) + 256 * (mi >> 4) + 128 * ((ki >> 4) & 1) + 4 * (ki >> 5)
+            else:  # lane = row, one 32-bit column per 32-wide K block
+                byte = 16 * mi + 4 * (ki >> 5) + 2 * ((ki >> 4) & 1)
+            E[tile * 2048 + byte] = bits & 0xFF
+            E[tile * 2048 + byte + 1] = bits >> 8
+    return E
+
+
+def test_metadata_layout_is_pinned(cuda, monkeypatch):
+    """The tcgen05 metadata format used by sparse24_compress (nibble p0 | p1<<2,
+    lanes m0 + 8 k1 + 16 m2 with rows r, r+8 in one word) is the only one of
+    these hypotheses under which the sparse GEMM matches the oracle, and the
+    GPU compress kernel reproduces the host-built buffer byte for byte."""
+    import torch
+    import kebab_b200 as kb
+    monkeypatch.setenv("KEBAB_SPARSE_CG", "1")
+    M = N = K = 128
+    A, B = O.fill_pair(M, N, K, seed=1, dist=O.NORMAL, scale_a=1.0, scale_b=1 / np.sqrt(K))
+    pr = _oracle_prune(A, M, K)
+    packed = np.empty(M * K // 2, np.uint16)
+    meta = np.empty(M * K // 2, np.uint32)
+    assert O.lib().kbo_pack_2of4(pr, packed, meta, M, K) == 0
+    ref = O.gemm(pr, B, M, N, K)
+    Bd = to_device(B, (N, K), O.F16, cuda)
+    Pd = to_device(packed, (M, K // 2), O.F16, cuda)
+    results = {}
+    for mode in ("p0|p1<<2", "p1|p0<<2", "code"):
+        for lanes in ("pair-rows", "row"):
+            E = torch.from_numpy(_host_e(meta, M, K, mode, lanes)).to(cuda)
+            C = kb.gemm_sparse24(Pd, E, Bd)
+            torch.cuda.synchronize()
+            results[(mode, lanes)] = O.check_tolerance(C.float().cpu().numpy().reshape(-1), ref)[0]
+    assert [k for k, ok in results.items() if ok] == [("p0|p1<<2", "pair-rows")]
+    packed_dev, E_dev = kb.sparse24_compress(to_device(pr, (M, K), O.F16, cuda))
+    assert np.array_equal(E_dev.cpu().numpy(), _host_e(meta, M, K, "p0|p1<<2", "pair-rows"))
+    assert np.array_equal(_u16(packed_dev), packed)
+
+
+def test_c5_sparse_8192_sampled(cuda):
+    """BASELINE config 5: A dense N(0,1) pruned 2:4, B N(0,1)/sqrt(K), 8192^3;
+    sampled rows + elements against the dense oracle GEMM of the pruned A."""
+    import torch
+    import kebab_b200 as kb
+    M = N = K = 8192
+    g = torch.Generator(device=cuda).manual_seed(5)
+    A = torch.randn((M, K), generator=g, device=cuda).half()
+    B = (torch.randn((N, K), generator=g, device=cuda) / K ** 0.5).half()
+    pr = kb.sparse24_prune(A)
+    packed, E = kb.sparse24_compress(pr)
+    C = torch.full((N, M), float("nan"), dtype=torch.float16, device=cuda)
+    kb.gemm_sparse24(packed, E, B, C)
+    torch.cuda.synchronize()
+    assert kb.device_status()[0] == kb.OK
+    rs = np.random.RandomState(0)
+    rows = np.array([0, M - 1, 4097])
+    ii = np.concatenate([np.repeat(rows, N), rs.randint(0, M, 20000)])
+    jj = np.concatenate([np.tile(np.arange(N), len(rows)), rs.randint(0, N, 20000)])
+    ref = O.gemm_elems(_u16(pr), _u16(B), ii, jj, M, N, K, O.F16)
+    dev = C.float()[torch.from_numpy(jj).to(cuda), torch.from_numpy(ii).to(cuda)].cpu().numpy()
+    ok, rel, worst = O.check_tolerance(dev, ref)
+    assert ok, "rel_fro=%.3e worst=%.3f" % (rel, worst)
