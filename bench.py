@@ -260,6 +260,8 @@ def main():
     M, N, K = args.m, args.n, args.k
     version = args.version
     resolved = kb.lib().kebab_resolve_version(version, kb.F16 if args.dtype == "fp16" else kb.BF16, M, N, K)
+    if args.workload == "sparse24":
+        resolved = "sparse24_cta_pair" if os.environ.get("KEBAB_SPARSE_CG", "2") != "1" else "sparse24_1cta"
     sparse = args.workload == "sparse24"
     workload = "%s_rc_%s_%dx%dx%d_msharded" % ("gemm_sparse24" if sparse else "gemm", args.dtype, M, N, K)
     stream = torch.cuda.current_stream()
@@ -454,7 +456,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
         "config": {"workload": workload, "M_per_rank": M, "M_global": M * world, "N": N, "K": K, "layout": "RC",
-                   "version": version, "rung": resolved, "rung_name": kb.version_name(resolved),
+                   "version": version, "rung": resolved,
+                   "rung_name": kb.version_name(resolved) if isinstance(resolved, int) else resolved,
                    "accumulate": "fp32", "inputs": "N(0,1)/sqrt(K), torch generator per rank",
                    "l2": "3 rotating input sets (%.0f MiB A+B per rank) > 126 MB L2" %
                          (NSETS * (M * K + N * K) * 2 / 2**20),
