@@ -63,20 +63,37 @@ __device__ __forceinline__ void partial_sort_top2(const float v[4], int& a, int&
   b = h1;
 }
 
+__device__ __forceinline__ uint2 prune_group(uint2 raw, int bf16) {
+  uint16_t e[4] = {(uint16_t)(raw.x & 0xFFFF), (uint16_t)(raw.x >> 16), (uint16_t)(raw.y & 0xFFFF),
+                   (uint16_t)(raw.y >> 16)};
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v[i] = fabsf(h2f(e[i], bf16));
+  int a, b;
+  partial_sort_top2(v, a, b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    if (i != a && i != b) e[i] = 0;
+  return make_uint2(e[0] | ((uint32_t)e[1] << 16), e[2] | ((uint32_t)e[3] << 16));
+}
+
+// Four groups (two 16-byte loads) per thread and iteration: enough bytes in
+// flight per thread to stream at HBM rate.
 __global__ void prune_kernel(const uint16_t* __restrict__ A, uint16_t* __restrict__ out, int64_t groups, int bf16) {
-  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups; g += (int64_t)gridDim.x * blockDim.x) {
-    const uint2 raw = reinterpret_cast<const uint2*>(A)[g];
-    uint16_t e[4] = {(uint16_t)(raw.x & 0xFFFF), (uint16_t)(raw.x >> 16), (uint16_t)(raw.y & 0xFFFF),
-                     (uint16_t)(raw.y >> 16)};
-    float v[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = fabsf(h2f(e[i], bf16));
-    int a, b;
-    partial_sort_top2(v, a, b);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (i != a && i != b) e[i] = 0;
-    reinterpret_cast<uint2*>(out)[g] = make_uint2(e[0] | ((uint32_t)e[1] << 16), e[2] | ((uint32_t)e[3] << 16));
+  const int64_t quads = groups / 4;
+  const uint4* src = reinterpret_cast<const uint4*>(A);
+  uint4* dst = reinterpret_cast<uint4*>(out);
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < quads; q += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 x = src[2 * q], y = src[2 * q + 1];
+    const uint2 a0 = prune_group(make_uint2(x.x, x.y), bf16), a1 = prune_group(make_uint2(x.z, x.w), bf16);
+    const uint2 b0 = prune_group(make_uint2(y.x, y.y), bf16), b1 = prune_group(make_uint2(y.z, y.w), bf16);
+    dst[2 * q] = make_uint4(a0.x, a0.y, a1.x, a1.y);
+    dst[2 * q + 1] = make_uint4(b0.x, b0.y, b1.x, b1.y);
+  }
+  // Tail (groups % 4), handled by the first threads of block 0.
+  if (blockIdx.x == 0 && threadIdx.x < groups % 4) {
+    const int64_t g = quads * 4 + threadIdx.x;
+    reinterpret_cast<uint2*>(out)[g] = prune_group(reinterpret_cast<const uint2*>(A)[g], bf16);
   }
 }
 
@@ -287,7 +304,7 @@ int kebab_sparse24_prune(kebab_dtype dtype, const void* A, void* A_pruned, int64
   int rc = check_common(dtype, A, A_pruned, M, K, 1, 4);
   if (rc) return rc;
   const int64_t groups = M * K / 4;
-  prune_kernel<<<grid_for(groups, 256), 256, 0, (cudaStream_t)stream>>>(
+  prune_kernel<<<grid_for(groups / 4 + 1, 256), 256, 0, (cudaStream_t)stream>>>(
       (const uint16_t*)A, (uint16_t*)A_pruned, groups, dtype == KEBAB_BF16);
   return launched("prune_kernel");
 }
