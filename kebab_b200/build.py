@@ -19,6 +19,10 @@ CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIBDIR = os.path.join(PKG, "lib")
 LIB = os.path.join(LIBDIR, "libkebab_b200.so")
+HARNESS = os.path.join(PKG, "harness")
+BINDIR = os.path.join(PKG, "bin")
+HARNESS_BINS = {"bench_gemm": ["bench_gemm.cpp", "config_parser.cpp"],
+                "runonce_gemm": ["runonce_gemm.cpp", "config_parser.cpp"]}
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
@@ -73,9 +77,29 @@ def build(force=False, jobs=None, verbose=False):
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s\n%s" % (r.stdout, r.stderr))
+    build_harness(force)
     if verbose:
         print(LIB)
     return LIB
+
+
+def build_harness(force=False):
+    """C++ harness binaries (config.yaml runner, single-launch runner) linked
+    against the in-tree library, cuBLAS and the CUDA runtime."""
+    os.makedirs(BINDIR, exist_ok=True)
+    hdrs = [os.path.join(HARNESS, f) for f in os.listdir(HARNESS) if f.endswith(".h")]
+    for name, srcs in HARNESS_BINS.items():
+        out = os.path.join(BINDIR, name)
+        deps = [os.path.join(HARNESS, s) for s in srcs] + hdrs + [LIB]
+        if not force and _mtime(out) > max(_mtime(d) for d in deps):
+            continue
+        cmd = ["g++", "-std=c++17", "-O2", "-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA_HOME, "include"),
+               *[os.path.join(HARNESS, s) for s in srcs], "-o", out, "-L", LIBDIR, "-lkebab_b200",
+               "-L", os.path.join(CUDA_HOME, "lib64"), "-lcublas", "-lcudart", "-Wl,-rpath,$ORIGIN/../lib",
+               "-Wl,-rpath," + os.path.join(CUDA_HOME, "lib64")]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError("harness build failed for %s:\n%s\n%s" % (name, r.stdout, r.stderr))
 
 
 if __name__ == "__main__":
