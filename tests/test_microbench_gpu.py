@@ -1,0 +1,35 @@
+"""sm_100a microbenchmark probes run, verify their one-shot result and report
+plausible numbers (bounded by the B200's nominal limits)."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("bf16", [False, True])
+def test_umma_once(cuda, cg, bf16):
+    from kebab_b200 import microbench as mb
+    d = mb.umma_once(bf16, cg)
+    assert d.shape == (128 * cg, 256)
+    assert np.all(d == 64.0)
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+def test_umma_throughput(cuda, cg):
+    from kebab_b200 import microbench as mb
+    tflops, cyc = mb.umma(cg, 256, iters=4000)
+    # nominal dense FP16 peak 2250 TFLOP/s at boost clock; measured must be real work
+    assert 300 < tflops < 2600, tflops
+    assert 32 <= cyc <= 2048, cyc
+
+
+def test_latency_tmem_tma(cuda):
+    import torch
+    from kebab_b200 import microbench as mb
+    assert 50 < mb.umma_latency(200) < 100000
+    b, t = mb.tmem_ld(2000)
+    assert b > 1 and t > 1
+    buf = torch.empty((1 << 14, 16384), dtype=torch.float16, device=cuda)  # 512 MiB > L2
+    gbs = mb.tma_load(buf, 128)
+    assert 500 < gbs < 12000, gbs
