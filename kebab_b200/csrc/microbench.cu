@@ -186,29 +186,29 @@ __global__ void __launch_bounds__(128, 1) tmem_ld_kernel(int iters, long long* c
 
 // Streams rows [blockIdx.x * rows_per_cta, ...) of a [rows][cols] FP16 array
 // through STAGES shared-memory slots of box_rows x 64 elements.
-constexpr int TMA_STAGES = 8;
+constexpr int TMA_STAGES = 8;  // slots allocated; `stages` of them are used
 __global__ void __launch_bounds__(64, 1) tma_load_kernel(const __grid_constant__ CUtensorMap tm, int rows_per_cta,
-                                                         int box_rows, int col_boxes, WaitCtx ctx) {
+                                                         int box_rows, int col_boxes, int stages, WaitCtx ctx) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* s = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stage_bytes = box_rows * 128;
-  uint64_t* full = reinterpret_cast<uint64_t*>(s + TMA_STAGES * stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(s + stages * stage_bytes);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TMA_STAGES; ++i) mbar_init(&full[i], 1);
+    for (int i = 0; i < stages; ++i) mbar_init(&full[i], 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (threadIdx.x != 0) return;
   const int row0 = blockIdx.x * rows_per_cta;
   const int nboxes = (rows_per_cta / box_rows) * col_boxes;
-  // Keep TMA_STAGES loads in flight; the "consumer" only waits for arrival.
-  for (int i = 0; i < nboxes + TMA_STAGES; ++i) {
-    if (i >= TMA_STAGES) {
-      const int j = i - TMA_STAGES;
-      if (!mbar_wait(&full[j % TMA_STAGES], (uint32_t)((j / TMA_STAGES) & 1), ctx, SITE_FULL)) return;
+  // Keep `stages` loads in flight; the "consumer" only waits for arrival.
+  for (int i = 0; i < nboxes + stages; ++i) {
+    if (i >= stages) {
+      const int j = i - stages;
+      if (!mbar_wait(&full[j % stages], (uint32_t)((j / stages) & 1), ctx, SITE_FULL)) return;
     }
     if (i < nboxes) {
-      const int st = i % TMA_STAGES;
+      const int st = i % stages;
       mbar_arrive_expect_tx(&full[st], stage_bytes);
       tma_load_2d(s + st * stage_bytes, &tm, &full[st], (i % col_boxes) * 64, row0 + (i / col_boxes) * box_rows);
     }
@@ -389,14 +389,16 @@ int kebab_mbench_tma_load(const void* buf, int64_t rows, int64_t cols, int box_r
   if (rows_per_cta <= 0) return fail(KEBAB_EINVAL, "tma_load: buffer too small for one box per SM");
   CUtensorMap tm;
   if ((rc = make_tmap_2d(&tm, buf, KEBAB_F16, rows, cols, cols, box_rows, 64, true))) return rc;
-  const int smem = 1024 + TMA_STAGES * box_rows * 128 + 8 * TMA_STAGES + 64;
+  // As many slots as fit in ~200 KB (at most 8): 8 x 8 KB boxes .. 6 x 32 KB boxes.
+  const int stages = std::max(2, std::min(TMA_STAGES, (200 * 1024) / (box_rows * 128)));
+  const int smem = 1024 + stages * box_rows * 128 + 8 * stages + 64;
   cudaError_t e = cudaFuncSetAttribute(tma_load_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   Events ev;
-  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), ctx);
+  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, ctx);
   if ((rc = finish(nullptr, "tma_load warm-up"))) return rc;
   cudaEventRecord(ev.a);
-  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), ctx);
+  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, ctx);
   cudaEventRecord(ev.b);
   if ((rc = finish(nullptr, "tma_load"))) return rc;
   *gbps = (double)rows_per_cta * grid * cols * 2.0 / (ev.ms() * 1e-3) / 1e9;
