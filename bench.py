@@ -42,7 +42,10 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", default="kebab", choices=["kebab", "reference"])
     p.add_argument("--version", type=int, default=120, help="ladder rung (120 = heuristic)")
-    p.add_argument("--m", type=int, default=8192, help="rows of A per rank")
+    p.add_argument("--m", type=int, default=8192, help="rows of A per rank (global M with --strong)")
+    p.add_argument("--strong", action="store_true",
+                   help="strong scaling: --m is the global M, row-sharded over the ranks (config 3: "
+                        "--strong --m 32768 --n 32768 --k 32768 --dtype bf16)")
     p.add_argument("--n", type=int, default=8192)
     p.add_argument("--k", type=int, default=8192)
     p.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
@@ -258,12 +261,20 @@ def main():
         dist.init_process_group("nccl", device_id=device)
     dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     M, N, K = args.m, args.n, args.k
+    M_global = M
+    if args.strong:
+        from kebab_b200.shard import row_block
+        M = row_block(M_global, world, rank).rows
+    else:
+        M_global = M * world
     version = args.version
     resolved = kb.lib().kebab_resolve_version(version, kb.F16 if args.dtype == "fp16" else kb.BF16, M, N, K)
     if args.workload == "sparse24":
         resolved = "sparse24_cta_pair" if os.environ.get("KEBAB_SPARSE_CG", "2") != "1" else "sparse24_1cta"
     sparse = args.workload == "sparse24"
-    workload = "%s_rc_%s_%dx%dx%d_msharded" % ("gemm_sparse24" if sparse else "gemm", args.dtype, M, N, K)
+    workload = "%s_rc_%s_%dx%dx%d_msharded%s" % ("gemm_sparse24" if sparse else "gemm", args.dtype,
+                                                  M_global if args.strong else M, N, K,
+                                                  "_strong" if args.strong else "")
     stream = torch.cuda.current_stream()
 
     # Inputs: A shards are generated per rank; B on rank 0, then broadcast.
@@ -416,12 +427,16 @@ def main():
         torch.cuda.synchronize()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         n_cb = args.steps  # same loop length as the timed region (same power state)
+        cb_sampler = ClockSampler(local)
+        cb_sampler.start()
+        time.sleep(0.3)
         c0.record(stream)
         for i in range(n_cb):
             torch.matmul(As[i % NSETS], Bs[i % NSETS].t())
         c1.record(stream)
         torch.cuda.synchronize()
-        cublas = {"value": flops_rank * n_cb / (c0.elapsed_time(c1) * 1e-3) / 1e12, "unit": UNIT,
+        cb_clocks = cb_sampler.stop()
+        cublas = {"value": flops_rank * n_cb / (c0.elapsed_time(c1) * 1e-3) / 1e12, "unit": UNIT, "clocks": cb_clocks,
                   "what": "torch.matmul (cuBLAS, FP32 accumulate) on the same inputs, 1 GPU, same number of back-to-back launches"}
 
     if rank != 0:
@@ -454,8 +469,9 @@ def main():
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
-        "config": {"workload": workload, "M_per_rank": M, "M_global": M * world, "N": N, "K": K, "layout": "RC",
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": args.dtype,
+        "data": "synthetic",
+        "config": {"workload": workload, "M_per_rank": M, "M_global": M_global, "N": N, "K": K, "layout": "RC",
                    "version": version, "rung": resolved,
                    "rung_name": kb.version_name(resolved) if isinstance(resolved, int) else resolved,
                    "accumulate": "fp32", "inputs": "N(0,1)/sqrt(K), torch generator per rank",

@@ -293,7 +293,8 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   args.K = (int)K;
   args.tiles_m = (int)((M + BM_T - 1) / BM_T);
   args.tiles_n = (int)((N + BN - 1) / BN);
-  args.group_m = 16;
+  args.group_m = 8;
+  args.epi_backoff_ns = 0;
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   auto kern = gemm_sparse_kernel<T, CG, STAGES>;
   static std::once_flag once[64];

@@ -65,6 +65,7 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
 struct UmmaArgs {
   int M, N, K;
   int tiles_m, tiles_n, group_m;
+  uint32_t epi_backoff_ns;  // sleep between polls of the epilogue's accumulator wait (0 = spin)
   WaitCtx ctx;
 };
 
@@ -259,7 +260,7 @@ __global__ void __launch_bounds__(192, 1)
       tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
       const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
       const int n0 = nb * BN;
-      if (!mbar_wait(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL)) break;
+      if (!mbar_wait_backoff(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL, args.epi_backoff_ns)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1

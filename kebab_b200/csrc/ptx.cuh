@@ -128,6 +128,28 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, const 
   }
 }
 
+// As mbar_wait, but sleeps `backoff_ns` between polls once the first few have
+// failed: for waits that are expected to be long (an epilogue waiting out a
+// whole main loop), where tight polling only burns issue slots and power.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, const WaitCtx& ctx, uint32_t site,
+                                                  uint32_t backoff_ns) {
+  if (backoff_ns == 0) return mbar_wait(bar, parity, ctx, site);
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait(addr, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(addr, parity)) return true;
+    if (it > 4) __nanosleep(backoff_ns);
+    if ((it & 15u) == 0u) {
+      if (aborted(ctx.status)) return false;
+      if (globaltimer() - t0 > ctx.timeout_ns) {
+        record_error(ctx.status, DEV_TIMEOUT, site);
+        return false;
+      }
+    }
+  }
+}
+
 // shared::cluster address of the same variable in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   uint32_t r;

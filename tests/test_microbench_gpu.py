@@ -31,7 +31,7 @@ def test_latency_tmem_tma(cuda):
     assert 50 < lat < 100000, lat
     b, t = mb.tmem_ld(2000)
     assert b > 1 and t > 1, (b, t)
-    buf = torch.empty((1 << 14, 16384), dtype=torch.float16, device=cuda)  # 512 MiB > L2
+    buf = torch.empty((1 << 16, 4096), dtype=torch.float16, device=cuda)  # 512 MiB > L2, 442 rows per SM
     for box in (64, 128, 256):
         gbs = mb.tma_load(buf, box)
         assert 500 < gbs < 12000, (box, gbs)
