@@ -22,7 +22,8 @@ LIB = os.path.join(LIBDIR, "libkebab_b200.so")
 HARNESS = os.path.join(PKG, "harness")
 BINDIR = os.path.join(PKG, "bin")
 HARNESS_BINS = {"bench_gemm": ["bench_gemm.cpp", "config_parser.cpp"],
-                "runonce_gemm": ["runonce_gemm.cpp", "config_parser.cpp"]}
+                "runonce_gemm": ["runonce_gemm.cpp", "config_parser.cpp"],
+                "simple_gemm": ["simple_gemm.cpp"]}
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 

@@ -37,6 +37,7 @@ const Rung kRungs[] = {
     {104, "tma_umma_tmem_warpspecialized_persistent", launch_v104_persistent},
     {105, "tma_umma_tmem_warpspecialized_persistent_2cta", launch_v105_pair},
     {106, "tma_umma_tmem_swapab_splitk_cluster_skinny", launch_v106_skinny},
+    {141, "tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c", launch_v105_pair},
 };
 
 const Rung* find_rung(int id) {
@@ -55,6 +56,7 @@ int map_reference_id(int v) {
     case 16: case 18: case 19: return 104;           // persistent scheduler
     case 8: case 9: case 10: case 11: case 12: return 105;  // cluster pairs
     case 20: return 120;                             // decomposition heuristic
+    case 41: return 141;                             // row-major C
     default: return v;
   }
 }
@@ -62,7 +64,7 @@ int map_reference_id(int v) {
 // The role of the reference's v20 heuristic (cuda_gemm.cu:25-77): choose a
 // decomposition from the tile count against the QUERIED SM count.
 // KEBAB_V120_MODE = dp | persistent | pair | heuristic (default).
-int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count) {
+int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
     std::string m(env);
@@ -70,11 +72,11 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count) {
     if (m == "DP" || m == "DATAPARALLEL") return 103;
     if (m == "PERSISTENT") return 104;
     if (m == "PAIR" || m == "2CTA") return 105;
-    if (m == "SKINNY" || m == "SPLITK") return 106;
+    if ((m == "SKINNY" || m == "SPLITK") && rc_colc) return 106;
   }
   // Decode-like shapes: too few 128-row tiles to occupy the GPU; stream B
   // with the swap-AB split-K rung.
-  if (M <= 256) return 106;
+  if (M <= 256 && rc_colc) return 106;
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
   if (pair_tiles >= sm_count / 2) return 105;
@@ -105,20 +107,24 @@ int kebab_list_versions(int* out, int cap) {
   return n;
 }
 
-int kebab_resolve_version(int version, kebab_dtype dtype, int64_t M, int64_t N, int64_t K) {
-  (void)dtype;
+static int resolve(int version, int64_t M, int64_t N, int64_t K, bool rc_colc) {
   int id = map_reference_id(version);
   if (id == 120) {
     DeviceInfo* d = nullptr;
     int rc = device_info(&d);
     int sms = rc == KEBAB_OK ? d->sm_count : 148;
-    id = choose_v120(M, N, K, sms);
+    id = choose_v120(M, N, K, sms, rc_colc);
   }
   if (!find_rung(id)) {
     fail(KEBAB_EINVAL, "unsupported version " + std::to_string(version));
     return -KEBAB_EINVAL;
   }
   return id;
+}
+
+int kebab_resolve_version(int version, kebab_dtype dtype, int64_t M, int64_t N, int64_t K) {
+  (void)dtype;
+  return resolve(version, M, N, K, true);
 }
 
 int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
@@ -133,12 +139,14 @@ int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t
   std::transform(mode.begin(), mode.end(), mode.begin(), [](unsigned char c) { return (char)std::toupper(c); });
   const char lhs = mode.size() >= 1 ? mode[0] : 'R';
   const char rhs = mode.size() >= 2 ? mode[1] : 'C';
-  if ((lhs != 'R' && lhs != 'C') || (rhs != 'R' && rhs != 'C'))
-    return fail(KEBAB_EINVAL, "opmode must be two of R/C, got \"" + mode + "\"");
-  const int id = kebab_resolve_version(version, dtype, M, N, K);
+  const char cl = mode.size() >= 3 ? mode[2] : 'C';
+  if ((lhs != 'R' && lhs != 'C') || (rhs != 'R' && rhs != 'C') || (cl != 'R' && cl != 'C') || mode.size() > 3)
+    return fail(KEBAB_EINVAL, "opmode must be two (or three, with C's layout) of R/C, got \"" + mode + "\"");
+  const bool c_row = (cl == 'R') || map_reference_id(version) == 141;
+  const int id = resolve(version, M, N, K, lhs == 'R' && rhs == 'C' && !c_row);
   if (id < 0) return -id;
   const Rung* r = find_rung(id);
-  GemmProblem p{(int)dtype, A, B, C, M, N, K, lhs, rhs, reinterpret_cast<cudaStream_t>(stream)};
+  GemmProblem p{(int)dtype, A, B, C, M, N, K, lhs, rhs, c_row, reinterpret_cast<cudaStream_t>(stream)};
   return r->launch(p);
 }
 
@@ -187,6 +195,49 @@ KEBAB_RUNG_LAUNCHER(gemm_v103_tma_umma_tmem_warpspecialized, 103)
 KEBAB_RUNG_LAUNCHER(gemm_v104_tma_umma_tmem_warpspecialized_persistent, 104)
 KEBAB_RUNG_LAUNCHER(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta, 105)
 KEBAB_RUNG_LAUNCHER(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny, 106)
+KEBAB_RUNG_LAUNCHER(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c, 141)
 #undef KEBAB_RUNG_LAUNCHER
 
 }  // namespace baseline
+
+// ---------------------------------------------------------------------------
+// CuTe-API alias (kebab/include/kebab/cute/gemm.h)
+// ---------------------------------------------------------------------------
+#include "kebab/cute/gemm.h"
+
+namespace kebab {
+namespace cute {
+
+namespace {
+std::string cute_mode(const char* opmode) {
+  std::string m(opmode ? opmode : "default");
+  std::transform(m.begin(), m.end(), m.begin(), [](unsigned char c) { return (char)std::toupper(c); });
+  if (m == "DEFAULT" || m.empty()) return "RR";
+  if (m.size() == 1) m += 'R';  // the CuTe path's default rhs
+  return m;
+}
+template <typename T>
+int dtype_of();
+template <>
+int dtype_of<__half>() { return KEBAB_F16; }
+template <>
+int dtype_of<__nv_bfloat16>() { return KEBAB_BF16; }
+template <>
+int dtype_of<float>() { return KEBAB_F32; }
+}  // namespace
+
+template <typename T>
+void gemm(const T* A, const T* B, T* C, int M, int N, int K, const char* opmode, int version, cudaStream_t stream) {
+  (void)version;  // every CuTe version resolves to the decomposition heuristic
+  const std::string mode = cute_mode(opmode);
+  const int rc = kebab_gemm((kebab_dtype)dtype_of<T>(), A, B, C, M, N, K, mode.c_str(), 120, stream);
+  if (rc != KEBAB_OK) std::fprintf(stderr, "ERROR: kebab::cute::gemm: %s\n", kebab_last_error());
+}
+
+template void gemm<__half>(const __half*, const __half*, __half*, int, int, int, const char*, int, cudaStream_t);
+template void gemm<__nv_bfloat16>(const __nv_bfloat16*, const __nv_bfloat16*, __nv_bfloat16*, int, int, int,
+                                  const char*, int, cudaStream_t);
+template void gemm<float>(const float*, const float*, float*, int, int, int, const char*, int, cudaStream_t);
+
+}  // namespace cute
+}  // namespace kebab

@@ -25,6 +25,11 @@
 //   CG=2              CTA pairs (cluster 2x1), tcgen05 cta_group::2,
 //                     256 x BN tiles; each CTA TMA-loads its own half of
 //                     A (rows) and of B (columns) — no multicast loads  (v105)
+// Layouts (LAYOUT bits): A row-major (K-major) or column-major (MN-major,
+// bit 1), B column-major (K-major) or row-major (MN-major, bit 2), C
+// column-major or row-major (bit 4). MN-major operands are staged as
+// 64-element x 64-K TMA boxes (128-byte swizzle) and described to the MMA
+// with LBO = 8 KB (next 64 elements along M/N) and SBO = 1 KB (next 8 K rows).
 // Every barrier wait is bounded (ptx.cuh); on expiry the kernel records an
 // error code, drains what it has in flight and returns.
 #pragma once
@@ -87,14 +92,27 @@ struct UmmaSmem {
   static_assert(BYTES + 1024 <= 232448, "shared memory budget exceeded");
 };
 
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT>
+enum : int { LAYOUT_A_MN = 1, LAYOUT_B_MN = 2, LAYOUT_C_ROW = 4 };
+
+// Operand descriptor for k-step `k` (16 elements of K) of a staged tile.
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
+  if constexpr (MN) return umma_desc(base + k * 2048, 8192, 1024, 2);  // 16 K rows = 2 x 1 KB groups
+  else return umma_desc_sw128(base + k * 32);                          // 16 K elements = 32 bytes
+}
+
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0>
 __global__ void __launch_bounds__(192, 1)
     gemm_umma_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const UmmaArgs args) {
   using L = UmmaSmem<BN, STAGES, CG>;
   constexpr int BM_T = 128 * CG;  // rows per (pair) tile
   constexpr int TMEM_COLS = 512;
-  constexpr uint32_t IDESC = umma_idesc_f16(BM_T, BN, ElemTraits<T>::kBf16);
+  constexpr bool A_MN = (LAYOUT & LAYOUT_A_MN) != 0;
+  constexpr bool B_MN = (LAYOUT & LAYOUT_B_MN) != 0;
+  constexpr bool C_ROW = (LAYOUT & LAYOUT_C_ROW) != 0;
+  constexpr uint32_t IDESC = umma_idesc_f16(BM_T, BN, ElemTraits<T>::kBf16) | (A_MN ? (1u << 15) : 0u) |
+                             (B_MN ? (1u << 16) : 0u);
   constexpr uint32_t TX_BYTES = (L::A_STAGE + L::B_STAGE) * CG;  // bytes landing on the issuing CTA's barrier
   static_assert(2 * BN <= TMEM_COLS, "two accumulators must fit in TMEM");
 
@@ -166,16 +184,22 @@ __global__ void __launch_bounds__(192, 1)
           }
           uint8_t* sA = smem + L::OFF_A + stage * L::A_STAGE;
           uint8_t* sB = smem + L::OFF_B + stage * L::B_STAGE;
-          if constexpr (CG == 1) {
-            mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-            tma_load_2d(sA, &tmA, &full[stage], kb * L::BK, m0);
-            tma_load_2d(sB, &tmB, &full[stage], kb * L::BK, n0);
-          } else {
-            if (leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-            const uint32_t fb = full_leader0 + stage * 8u;
-            tma_load_2d_pair(sA, &tmA, fb, kb * L::BK, m0);
-            tma_load_2d_pair(sB, &tmB, fb, kb * L::BK, n0);
-          }
+          // K-major tiles are one box (x = K, y = rows); MN-major tiles are
+          // boxes of 64 rows-or-columns each (x = M or N, y = K).
+          auto load = [&](uint8_t* dst, const CUtensorMap* tm, int rows0, int nrows, bool mn) {
+            if (!mn) {
+              if constexpr (CG == 1) tma_load_2d(dst, tm, &full[stage], kb * L::BK, rows0);
+              else tma_load_2d_pair(dst, tm, full_leader0 + stage * 8u, kb * L::BK, rows0);
+            } else {
+              for (int j = 0; j < nrows / 64; ++j) {
+                if constexpr (CG == 1) tma_load_2d(dst + j * 8192, tm, &full[stage], rows0 + j * 64, kb * L::BK);
+                else tma_load_2d_pair(dst + j * 8192, tm, full_leader0 + stage * 8u, rows0 + j * 64, kb * L::BK);
+              }
+            }
+          };
+          if (CG == 1 || leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+          load(sA, &tmA, m0, 128, A_MN);
+          load(sB, &tmB, n0, BN / CG, B_MN);
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -217,8 +241,8 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
 #pragma unroll
           for (int k = 0; k < L::BK / 16; ++k) {
-            const uint64_t ad = umma_desc_sw128(a_addr + k * 32);
-            const uint64_t bd = umma_desc_sw128(b_addr + k * 32);
+            const uint64_t ad = operand_desc<A_MN>(a_addr, k);
+            const uint64_t bd = operand_desc<B_MN>(b_addr, k);
             if constexpr (CG == 1)
               umma_f16_cg1(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
             else
@@ -280,12 +304,27 @@ __global__ void __launch_bounds__(192, 1)
         T* buf = stage_c + (sub & 1) * (32 * 32);
         if (lane == 0) tma_store_wait_read<1>();  // the store that used `buf` has read it
         __syncwarp();
+        if constexpr (!C_ROW) {
+          // [column][row] sub-tile: for each column the warp writes 64 contiguous bytes.
 #pragma unroll
-        for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+          for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+        } else {
+          // [row][column] sub-tile, 64-byte rows in the TMA 64-byte swizzle:
+          // 16-byte chunk c of row r sits at chunk c ^ ((r >> 1) & 3).
+          uint4* row = reinterpret_cast<uint4*>(buf + lane * 32);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            alignas(16) T h[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) h[j] = ElemTraits<T>::cvt(__uint_as_float(v[q4 * 8 + j]));
+            row[q4 ^ ((lane >> 1) & 3)] = *reinterpret_cast<const uint4*>(h);
+          }
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
+          if constexpr (!C_ROW) tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
+          else tma_store_2d(&tmC, buf, n0 + c * 32, m_rows);
           tma_store_commit();
         }
         ++sub;

@@ -1,4 +1,7 @@
-// Launchers of the warp-specialised tcgen05 rungs (v103, v104, v105).
+// Host launch template of the warp-specialised tcgen05 rungs (v103, v104,
+// v105) for every operand layout; each rung instantiates it in its own
+// translation unit (gemm_v103_ws.cu, gemm_v104_persistent.cu, gemm_v105_pair.cu).
+#pragma once
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -7,15 +10,13 @@
 #include "internal.h"
 
 namespace kb {
+namespace umma_launch {
 
-namespace {
-
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT>
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT>
 int launch_umma(const GemmProblem& p) {
   using L = UmmaSmem<BN, STAGES, CG>;
   int rc = check_tma_shapes(p);
   if (rc) return rc;
-  if (p.lhs != 'R' || p.rhs != 'C') return fail(KEBAB_ENOTSUP, "this rung implements opmode RC only");
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   UmmaArgs args;
@@ -23,12 +24,27 @@ int launch_umma(const GemmProblem& p) {
 
   constexpr int BM_T = 128 * CG;
   CUtensorMap tA, tB, tC;
-  // A: M x K row-major; box = 128 rows x 64 K (one CTA's half of a pair tile).
-  if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.M, p.K, p.K, 128, 64, true))) return rc;
-  // B: column-major K x N = row-major N x K; box = BN/CG columns x 64 K.
-  if ((rc = make_tmap_2d(&tB, p.B, p.dtype, p.N, p.K, p.K, BN / CG, 64, true))) return rc;
-  // C: column-major M x N = row-major N x M; box = 32 columns x 32 rows.
-  if ((rc = make_tmap_2d(&tC, p.C, p.dtype, p.N, p.M, p.M, 32, 32, false))) return rc;
+  if (!(LAYOUT & LAYOUT_A_MN)) {
+    // A row-major M x K: box = 128 rows x 64 K (one CTA's rows of a tile).
+    if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.M, p.K, p.K, 128, 64, true))) return rc;
+  } else {
+    // A column-major M x K = row-major K x M: boxes of 64 K rows x 64 M.
+    if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.K, p.M, p.M, 64, 64, true))) return rc;
+  }
+  if (!(LAYOUT & LAYOUT_B_MN)) {
+    // B column-major K x N = row-major N x K: box = BN/CG columns x 64 K.
+    if ((rc = make_tmap_2d(&tB, p.B, p.dtype, p.N, p.K, p.K, BN / CG, 64, true))) return rc;
+  } else {
+    // B row-major K x N: boxes of 64 K rows x 64 N.
+    if ((rc = make_tmap_2d(&tB, p.B, p.dtype, p.K, p.N, p.N, 64, 64, true))) return rc;
+  }
+  if (!(LAYOUT & LAYOUT_C_ROW)) {
+    // C column-major M x N = row-major N x M: box = 32 columns x 32 rows.
+    if ((rc = make_tmap_2d(&tC, p.C, p.dtype, p.N, p.M, p.M, 32, 32, false))) return rc;
+  } else {
+    // C row-major M x N: box = 32 rows x 32 columns (64-byte rows, 64-byte swizzle).
+    if ((rc = make_tmap_2d_sw(&tC, p.C, p.dtype, p.M, p.N, p.N, 32, 32, 64))) return rc;
+  }
 
   args.M = (int)p.M;
   args.N = (int)p.N;
@@ -52,7 +68,7 @@ int launch_umma(const GemmProblem& p) {
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
 
-  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT>;
+  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT>;
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
   const int di = dev->device & 63;
@@ -108,16 +124,30 @@ int launch_umma(const GemmProblem& p) {
   return KEBAB_OK;
 }
 
-template <int CG, bool PERSISTENT, int STAGES>
+
+
+template <int CG, bool PERSISTENT, int STAGES, int LAYOUT>
 int dispatch_dtype(const GemmProblem& p) {
-  if (p.dtype == KEBAB_F16) return launch_umma<__half, 256, STAGES, CG, PERSISTENT>(p);
-  return launch_umma<__nv_bfloat16, 256, STAGES, CG, PERSISTENT>(p);
+  if (p.dtype == KEBAB_F16) return launch_umma<__half, 256, STAGES, CG, PERSISTENT, LAYOUT>(p);
+  return launch_umma<__nv_bfloat16, 256, STAGES, CG, PERSISTENT, LAYOUT>(p);
 }
 
-}  // namespace
+// Layout from the problem: A column-major, B row-major, C row-major bits.
+template <int CG, bool PERSISTENT, int STAGES>
+int dispatch(const GemmProblem& p) {
+  const int layout = (p.lhs == 'C' ? LAYOUT_A_MN : 0) | (p.rhs == 'R' ? LAYOUT_B_MN : 0) |
+                     (p.c_row ? LAYOUT_C_ROW : 0);
+  switch (layout) {
+    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0>(p);
+    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1>(p);
+    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2>(p);
+    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3>(p);
+    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4>(p);
+    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5>(p);
+    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6>(p);
+    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7>(p);
+  }
+}
 
-int launch_v103_ws(const GemmProblem& p) { return dispatch_dtype<1, false, 4>(p); }
-int launch_v104_persistent(const GemmProblem& p) { return dispatch_dtype<1, true, 4>(p); }
-int launch_v105_pair(const GemmProblem& p) { return dispatch_dtype<2, true, 6>(p); }
-
+}  // namespace umma_launch
 }  // namespace kb

@@ -111,7 +111,8 @@ template <typename T>
 int launch(const GemmProblem& p) {
   int rc = check_tma_shapes(p);
   if (rc) return rc;
-  if (p.lhs != 'R' || p.rhs != 'C') return fail(KEBAB_ENOTSUP, "this rung implements opmode RC only");
+  if (p.lhs != 'R' || p.rhs != 'C' || p.c_row)
+    return fail(KEBAB_ENOTSUP, "this rung implements opmode RC with column-major C only");
   WaitCtx ctx;
   if ((rc = wait_ctx(&ctx))) return rc;
   CUtensorMap tA, tB;

@@ -203,7 +203,8 @@ int launch(const GemmProblem& p, int splits_override) {
   using L = SkinnySmem<BNM>;
   int rc = check_tma_shapes(p);
   if (rc) return rc;
-  if (p.lhs != 'R' || p.rhs != 'C') return fail(KEBAB_ENOTSUP, "this rung implements opmode RC only");
+  if (p.lhs != 'R' || p.rhs != 'C' || p.c_row)
+    return fail(KEBAB_ENOTSUP, "this rung implements opmode RC with column-major C only");
   DeviceInfo* dev = nullptr;
   if ((rc = device_info(&dev))) return rc;
   WaitCtx ctx;

@@ -34,6 +34,9 @@ int wait_ctx(WaitCtx* out);
 // swizzle128: 128-byte swizzle (box_cols * 2 must be 128).
 int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
                  uint32_t box_rows, uint32_t box_cols, bool swizzle128);
+// Same with the swizzle given in bytes: 0 (none), 32, 64 or 128.
+int make_tmap_2d_sw(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
+                    uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
 // Problem description passed to every launcher.
 struct GemmProblem {
@@ -43,6 +46,7 @@ struct GemmProblem {
   void* C;
   int64_t M, N, K;
   char lhs, rhs;  // 'R'/'C' storage of A and B
+  bool c_row = false;  // C row-major (ldC = N) instead of column-major (ldC = M)
   cudaStream_t stream;
 };
 
@@ -57,7 +61,8 @@ int launch_v106_skinny(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and
-// row pitches (K % 8 == 0 for A/B rows, M % 8 == 0 for C columns).
+// 16-byte row pitches of A, B and C in their storage layouts (RC: K % 8 and
+// M % 8; a column-major A needs M % 8, a row-major B or C needs N % 8).
 int check_tma_shapes(const GemmProblem& p);
 
 }  // namespace kb

@@ -105,6 +105,11 @@ static int get_encoder() {
 
 int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
                  uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  return make_tmap_2d_sw(out, base, dtype, rows, cols, ld, box_rows, box_cols, swizzle128 ? 128 : 0);
+}
+
+int make_tmap_2d_sw(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
+                    uint32_t box_rows, uint32_t box_cols, int swizzle_bytes) {
   int rc = get_encoder();
   if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
@@ -116,7 +121,10 @@ int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, u
   cuuint32_t estr[2] = {1, 1};
   CUtensorMapDataType t = dtype == KEBAB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = g_encode(out, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                        : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KEBAB_EINVAL, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
   return KEBAB_OK;
@@ -125,8 +133,15 @@ int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, u
 int check_tma_shapes(const GemmProblem& p) {
   if ((reinterpret_cast<uintptr_t>(p.A) | reinterpret_cast<uintptr_t>(p.B) | reinterpret_cast<uintptr_t>(p.C)) & 15u)
     return fail(KEBAB_EINVAL, "A, B and C must be 16-byte aligned for the TMA rungs");
-  if (p.K % 8 != 0) return fail(KEBAB_EINVAL, "K must be a multiple of 8 (16-byte rows of A and B) for the TMA rungs");
-  if (p.M % 8 != 0) return fail(KEBAB_EINVAL, "M must be a multiple of 8 (16-byte columns of C) for the TMA rungs");
+  const bool needK = p.lhs == 'R' || p.rhs == 'C';
+  const bool needM = p.lhs == 'C' || !p.c_row;
+  const bool needN = p.rhs == 'R' || p.c_row;
+  if (needK && p.K % 8 != 0)
+    return fail(KEBAB_EINVAL, "K must be a multiple of 8 (16-byte rows of A / B) for the TMA rungs");
+  if (needM && p.M % 8 != 0)
+    return fail(KEBAB_EINVAL, "M must be a multiple of 8 (16-byte pitch of A or C) for the TMA rungs");
+  if (needN && p.N % 8 != 0)
+    return fail(KEBAB_EINVAL, "N must be a multiple of 8 (16-byte pitch of B or C) for the TMA rungs");
   if (p.M > INT32_MAX || p.N > INT32_MAX || p.K > INT32_MAX)
     return fail(KEBAB_EINVAL, "each of M, N, K must fit in int32 for the TMA rungs");
   return KEBAB_OK;
