@@ -25,7 +25,7 @@ def _run(cuda, M, N, K, opmode, version, dtype=O.F16, seed=0):
     A2 = A.reshape(M, K)          # row-major A
     B2 = B.reshape(N, K)          # column-major B (stored N x K)
     lhs, rhs = opmode[0], opmode[1]
-    c_row = len(opmode) > 2 and opmode[2] == "R"
+    c_row = (len(opmode) > 2 and opmode[2] == "R") or version == 141
     a_store = A2 if lhs == "R" else np.ascontiguousarray(A2.T)  # col-major A = K x M row-major
     b_store = B2 if rhs == "C" else np.ascontiguousarray(B2.T)  # row-major B = K x N
     td = torch_dtype(dtype)
