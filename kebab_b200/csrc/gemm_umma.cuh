@@ -71,6 +71,7 @@ struct UmmaArgs {
   int M, N, K;
   int tiles_m, tiles_n, group_m;
   uint32_t epi_backoff_ns;  // sleep between polls of the epilogue's accumulator wait (0 = spin)
+  int l2_hint;              // 0: no hint; bits 0..1 policy of A, bits 2..3 of B (1 last, 2 first, 3 normal)
   WaitCtx ctx;
 };
 
@@ -108,13 +109,17 @@ __global__ void __launch_bounds__(192, 1)
   using L = UmmaSmem<BN, STAGES, CG>;
   constexpr int BM_T = 128 * CG;  // rows per (pair) tile
   constexpr int TMEM_COLS = 512;
+  // BN = 512 (pairs only): two N = 256 MMAs per k-step share the A tile; the
+  // 512-column accumulator fills TMEM, so it is single-buffered.
+  constexpr int NSUB = BN / 256 > 1 ? BN / 256 : 1;
+  constexpr int ACCS = (2 * BN <= TMEM_COLS) ? 2 : 1;
+  static_assert(BN <= 256 || (BN == 512 && CG == 2), "BN = 512 needs CTA pairs");
   constexpr bool A_MN = (LAYOUT & LAYOUT_A_MN) != 0;
   constexpr bool B_MN = (LAYOUT & LAYOUT_B_MN) != 0;
   constexpr bool C_ROW = (LAYOUT & LAYOUT_C_ROW) != 0;
-  constexpr uint32_t IDESC = umma_idesc_f16(BM_T, BN, ElemTraits<T>::kBf16) | (A_MN ? (1u << 15) : 0u) |
+  constexpr uint32_t IDESC = umma_idesc_f16(BM_T, BN / NSUB, ElemTraits<T>::kBf16) | (A_MN ? (1u << 15) : 0u) |
                              (B_MN ? (1u << 16) : 0u);
   constexpr uint32_t TX_BYTES = (L::A_STAGE + L::B_STAGE) * CG;  // bytes landing on the issuing CTA's barrier
-  static_assert(2 * BN <= TMEM_COLS, "two accumulators must fit in TMEM");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -186,8 +191,13 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sB = smem + L::OFF_B + stage * L::B_STAGE;
           // K-major tiles are one box (x = K, y = rows); MN-major tiles are
           // boxes of 64 rows-or-columns each (x = M or N, y = K).
-          auto load = [&](uint8_t* dst, const CUtensorMap* tm, int rows0, int nrows, bool mn) {
-            if (!mn) {
+          auto load = [&](uint8_t* dst, const CUtensorMap* tm, int rows0, int nrows, bool mn, int hint) {
+            if (!mn && hint) {
+              const uint64_t pol = hint == 1 ? l2_policy_evict_last()
+                                   : hint == 2 ? l2_policy_evict_first() : l2_policy_evict_normal();
+              if constexpr (CG == 1) tma_load_2d_hint(dst, tm, &full[stage], kb * L::BK, rows0, pol);
+              else tma_load_2d_pair_hint(dst, tm, full_leader0 + stage * 8u, kb * L::BK, rows0, pol);
+            } else if (!mn) {
               if constexpr (CG == 1) tma_load_2d(dst, tm, &full[stage], kb * L::BK, rows0);
               else tma_load_2d_pair(dst, tm, full_leader0 + stage * 8u, kb * L::BK, rows0);
             } else {
@@ -198,8 +208,8 @@ __global__ void __launch_bounds__(192, 1)
             }
           };
           if (CG == 1 || leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-          load(sA, &tmA, m0, 128, A_MN);
-          load(sB, &tmB, n0, BN / CG, B_MN);
+          load(sA, &tmA, m0, 128, A_MN, args.l2_hint & 3);
+          load(sB, &tmB, n0, BN / CG, B_MN, (args.l2_hint >> 2) & 3);
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -242,11 +252,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int k = 0; k < L::BK / 16; ++k) {
             const uint64_t ad = operand_desc<A_MN>(a_addr, k);
-            const uint64_t bd = operand_desc<B_MN>(b_addr, k);
-            if constexpr (CG == 1)
-              umma_f16_cg1(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
-            else
-              umma_f16_cg2(d_tmem, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+#pragma unroll
+            for (int sub = 0; sub < NSUB; ++sub) {
+              // Sub-MMA `sub` reads rows [128 sub, 128 sub + 128) of each CTA's B tile.
+              const uint64_t bd = operand_desc<B_MN>(b_addr + sub * (128 * L::BK * 2), k);
+              if constexpr (CG == 1)
+                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+              else
+                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+            }
           }
           any_issued = true;
           if constexpr (CG == 1) umma_commit_cg1(&empty[stage]);
@@ -259,8 +273,10 @@ __global__ void __launch_bounds__(192, 1)
         if (!ok) break;
         if constexpr (CG == 1) umma_commit_cg1(&tmem_full[acc]);
         else umma_commit_cg2_mc(&tmem_full[acc], 0x3);
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1u;
+        if (++acc == ACCS) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
       }
       if (!ok && any_issued) {
         // Abort: wait for the MMAs already issued before TMEM is freed.
@@ -323,14 +339,21 @@ __global__ void __launch_bounds__(192, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (!C_ROW) tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
-          else tma_store_2d(&tmC, buf, n0 + c * 32, m_rows);
+          // Global column of accumulator column d = 32 c. With BN = 512 each CTA of
+          // the pair holds 256 contiguous B rows, so sub-MMA s covers columns
+          // n0 + 128 s + [0, 128) (leader) and n0 + 256 + 128 s + [0, 128) (peer).
+          const int d = c * 32;
+          const int gcol = NSUB == 1 ? n0 + d : n0 + ((d & 255) >= 128 ? 256 : 0) + 128 * (d >> 8) + (d & 127);
+          if constexpr (!C_ROW) tma_store_2d(&tmC, buf, m_rows, gcol);
+          else tma_store_2d(&tmC, buf, gcol, m_rows);
           tma_store_commit();
         }
         ++sub;
       }
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1u;
+      if (++acc == ACCS) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
     if (lane == 0) tma_store_wait_all<0>();
     __syncwarp();

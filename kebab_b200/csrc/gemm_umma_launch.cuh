@@ -65,6 +65,12 @@ int launch_umma(const GemmProblem& p) {
     return (e && *e) ? (uint32_t)std::atoi(e) : 0u;
   }();
   args.epi_backoff_ns = backoff_env;
+  // L2 eviction hints of the A / B loads (KEBAB_L2_HINT, see UmmaArgs; default none).
+  static const int hint_env = [] {
+    const char* e = std::getenv("KEBAB_L2_HINT");
+    return (e && *e) ? std::atoi(e) : 0;
+  }();
+  args.l2_hint = hint_env;
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
 
@@ -126,26 +132,26 @@ int launch_umma(const GemmProblem& p) {
 
 
 
-template <int CG, bool PERSISTENT, int STAGES, int LAYOUT>
+template <int CG, bool PERSISTENT, int STAGES, int LAYOUT, int BN>
 int dispatch_dtype(const GemmProblem& p) {
-  if (p.dtype == KEBAB_F16) return launch_umma<__half, 256, STAGES, CG, PERSISTENT, LAYOUT>(p);
-  return launch_umma<__nv_bfloat16, 256, STAGES, CG, PERSISTENT, LAYOUT>(p);
+  if (p.dtype == KEBAB_F16) return launch_umma<__half, BN, STAGES, CG, PERSISTENT, LAYOUT>(p);
+  return launch_umma<__nv_bfloat16, BN, STAGES, CG, PERSISTENT, LAYOUT>(p);
 }
 
 // Layout from the problem: A column-major, B row-major, C row-major bits.
-template <int CG, bool PERSISTENT, int STAGES>
+template <int CG, bool PERSISTENT, int STAGES, int BN = 256>
 int dispatch(const GemmProblem& p) {
   const int layout = (p.lhs == 'C' ? LAYOUT_A_MN : 0) | (p.rhs == 'R' ? LAYOUT_B_MN : 0) |
                      (p.c_row ? LAYOUT_C_ROW : 0);
   switch (layout) {
-    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0>(p);
-    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1>(p);
-    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2>(p);
-    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3>(p);
-    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4>(p);
-    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5>(p);
-    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6>(p);
-    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7>(p);
+    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0, BN>(p);
+    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1, BN>(p);
+    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2, BN>(p);
+    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3, BN>(p);
+    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4, BN>(p);
+    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5, BN>(p);
+    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6, BN>(p);
+    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7, BN>(p);
   }
 }
 

@@ -58,6 +58,7 @@ int launch_v103_ws(const GemmProblem& p);
 int launch_v104_persistent(const GemmProblem& p);
 int launch_v105_pair(const GemmProblem& p);
 int launch_v106_skinny(const GemmProblem& p);
+int launch_v107_pair_wide(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and

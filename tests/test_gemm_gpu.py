@@ -11,7 +11,7 @@ from gemm_util import assert_close, inputs, run
 
 pytestmark = pytest.mark.gpu
 
-TC_RUNGS = [101, 102, 103, 104, 105]
+TC_RUNGS = [101, 102, 103, 104, 105, 107]
 ALL_RUNGS = [1] + TC_RUNGS
 
 
@@ -34,7 +34,7 @@ def test_ragged_shapes(cuda, version, shape):
     assert_close(run(A, B, M, N, K, O.F16, version, cuda), ref, "v%d %s" % (version, shape))
 
 
-@pytest.mark.parametrize("version", [103, 104, 105, 120])
+@pytest.mark.parametrize("version", [103, 104, 105, 107, 120])
 @pytest.mark.parametrize("dtype", [O.F16, O.BF16])
 def test_2048_full(cuda, version, dtype):
     M = N = K = 2048
@@ -43,7 +43,7 @@ def test_2048_full(cuda, version, dtype):
     assert_close(run(A, B, M, N, K, dtype, version, cuda), ref, "v%d" % version, dtype)
 
 
-@pytest.mark.parametrize("version", [104, 105])
+@pytest.mark.parametrize("version", [104, 105, 107])
 def test_deterministic(cuda, version):
     M, N, K = 1024, 1536, 2048
     A, B = inputs(M, N, K, seed=5)
@@ -125,7 +125,7 @@ def _sampled_check(M, N, K, dtype, version, cuda, scale_a, scale_b, nrows=4, nel
     assert ok, "v%d %dx%dx%d: rel_fro=%.3e worst=%.3f" % (version, M, N, K, rel, worst)
 
 
-@pytest.mark.parametrize("version", [104, 105])
+@pytest.mark.parametrize("version", [104, 105, 107])
 def test_c2_8192_sampled(cuda, version):
     _sampled_check(8192, 8192, 8192, O.F16, version, cuda, 1 / np.sqrt(8192), 1 / np.sqrt(8192))
 
