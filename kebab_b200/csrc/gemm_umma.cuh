@@ -6,14 +6,15 @@
 // specialised WGMMA kernels (kebab/lib/cuda/cuda_gemm_v4_* ... v19_*, hot loop
 // described at cuda_gemm_v10_*:313-473): same operator, different machine.
 //
-// Roles (192 threads, 6 warps):
+// Roles (192 threads = 6 warps; 320 = 10 warps for the 512-column tile):
 //   warp 0        TMA producer: one elected lane streams K-blocks of A and B
 //                 into a STAGES-deep shared-memory ring (128-byte swizzle).
 //   warp 1        TMEM owner + MMA issuer: allocates 512 TMEM columns (two
 //                 BN-column FP32 accumulators), one lane issues
 //                 tcgen05.mma (kind::f16, 128 x BN x 16, or 256 x BN x 16 over
 //                 a CTA pair) and tcgen05.commit to release ring slots.
-//   warps 2..5    epilogue: tcgen05.ld 32 columns at a time, convert, stage
+//   warps 2..5    epilogue (warps 2..9 with two warps per TMEM lane quarter
+//                 for BN = 512): tcgen05.ld 32 columns at a time, convert, stage
 //                 32 x 32 column-major sub-tiles in shared memory and write
 //                 them with TMA stores; the accumulator is released as soon
 //                 as it has been read, so the next tile's MMAs overlap the
@@ -75,6 +76,14 @@ struct UmmaArgs {
   WaitCtx ctx;
 };
 
+// Epilogue warps: 4 (one per TMEM lane quarter), or 8 for the 512-column
+// accumulator (two per quarter, each draining half of the columns).
+template <int BN>
+struct UmmaEpi {
+  static constexpr int WARPS = BN > 256 ? 8 : 4;
+  static constexpr int THREADS = 64 + 32 * WARPS;
+};
+
 template <int BN, int STAGES, int CG>
 struct UmmaSmem {
   static constexpr int BM = 128;  // rows of A per CTA
@@ -82,7 +91,7 @@ struct UmmaSmem {
   static constexpr int A_STAGE = BM * BK * 2;
   static constexpr int B_STAGE = (BN / CG) * BK * 2;
   static constexpr int C_SUB = 32 * 32 * 2;  // one 32x32 staging sub-tile
-  static constexpr int C_BYTES = 4 * 2 * C_SUB;
+  static constexpr int C_BYTES = UmmaEpi<BN>::WARPS * 2 * C_SUB;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
   static constexpr int OFF_C = OFF_B + STAGES * B_STAGE;
@@ -103,7 +112,7 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
 }
 
 template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     gemm_umma_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const UmmaArgs args) {
   using L = UmmaSmem<BN, STAGES, CG>;
@@ -147,7 +156,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4 * CG);
+      mbar_init(&tmem_empty[a], UmmaEpi<BN>::WARPS * CG);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -289,7 +298,9 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const int q = warp & 3;       // TMEM lane quarter this warp may access
-    const int ew = warp - 2;      // epilogue warp index 0..3 (staging buffers)
+    const int ew = warp - 2;      // epilogue warp index (staging buffers)
+    constexpr int CHUNKS = BN / 32 / (UmmaEpi<BN>::WARPS / 4);  // 32-column chunks per warp
+    const int c0 = (ew / 4) * CHUNKS;                           // this warp's first chunk
     T* stage_c = reinterpret_cast<T*>(smem + L::OFF_C + ew * 2 * L::C_SUB);
     const uint32_t tmem_empty_leader0 = (CG == 2) ? mapa_shared(smem_u32(&tmem_empty[0]), 0) : 0u;
     int acc = 0;
@@ -304,11 +315,11 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c0; c < c0 + CHUNKS; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), v);
         tmem_ld_wait();
-        if (c == BN / 32 - 1) {
+        if (c == c0 + CHUNKS - 1) {
           // Accumulator fully read: hand it back to the MMA issuer.
           tc_fence_before();
           __syncwarp();

@@ -92,7 +92,7 @@ int launch_umma(const GemmProblem& p) {
       if (max_active[di] == 0) {
         cudaLaunchConfig_t qc = {};
         qc.gridDim = dim3(CG * max_clusters, 1, 1);
-        qc.blockDim = dim3(192, 1, 1);
+        qc.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
         qc.dynamicSmemBytes = L::ALLOC;
         cudaLaunchAttribute qa[1];
         qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -115,7 +115,7 @@ int launch_umma(const GemmProblem& p) {
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = p.stream;
   cudaLaunchAttribute attr[1];
