@@ -64,7 +64,7 @@ int map_reference_id(int v) {
 
 // The role of the reference's v20 heuristic (cuda_gemm.cu:25-77): choose a
 // decomposition from the tile count against the QUERIED SM count.
-// KEBAB_V120_MODE = dp | persistent | pair | heuristic (default).
+// KEBAB_V120_MODE = dp | persistent | pair | wide | skinny | heuristic (default).
 int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
@@ -73,14 +73,21 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
     if (m == "DP" || m == "DATAPARALLEL") return 103;
     if (m == "PERSISTENT") return 104;
     if (m == "PAIR" || m == "2CTA") return 105;
+    if (m == "WIDE" || m == "PAIRWIDE") return 107;
     if ((m == "SKINNY" || m == "SPLITK") && rc_colc) return 106;
   }
   // Decode-like shapes: too few 128-row tiles to occupy the GPU; stream B
   // with the swap-AB split-K rung.
   if (M <= 256 && rc_colc) return 106;
+  const int64_t pairs = sm_count / 2;
+  const int64_t wide_tiles = ((M + 255) / 256) * ((N + 511) / 512);
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  // 256 x 512 pair tiles cut operand traffic per FLOP by a quarter (lower
+  // power, higher clock under the cap); worth it with at least two waves and
+  // little N padding.
+  if (wide_tiles >= 2 * pairs && N % 512 == 0) return 107;
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
-  if (pair_tiles >= sm_count / 2) return 105;
+  if (pair_tiles >= pairs) return 105;
   return 104;
 }
 
