@@ -42,12 +42,14 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", default="kebab", choices=["kebab", "reference"])
     p.add_argument("--version", type=int, default=120, help="ladder rung (120 = heuristic)")
-    p.add_argument("--m", type=int, default=8192, help="rows of A per rank (global M with --strong)")
+    # Capitalised flags: under torchrun a lowercase --m is taken as an
+    # abbreviation of torchrun's own options.
+    p.add_argument("--M", "--m", dest="m", type=int, default=8192, help="rows of A per rank (global M with --strong)")
     p.add_argument("--strong", action="store_true",
-                   help="strong scaling: --m is the global M, row-sharded over the ranks (config 3: "
-                        "--strong --m 32768 --n 32768 --k 32768 --dtype bf16)")
-    p.add_argument("--n", type=int, default=8192)
-    p.add_argument("--k", type=int, default=8192)
+                   help="strong scaling: --M is the global M, row-sharded over the ranks (config 3: "
+                        "--strong --M 32768 --N 32768 --K 32768 --dtype bf16)")
+    p.add_argument("--N", "--n", dest="n", type=int, default=8192)
+    p.add_argument("--K", "--k", dest="k", type=int, default=8192)
     p.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"])
     p.add_argument("--workload", default="dense", choices=["dense", "sparse24"],
                    help="dense GEMM (BASELINE config 2) or 2:4 sparse GEMM (config 5)")
