@@ -3,6 +3,7 @@
 // translation unit (gemm_v103_ws.cu, gemm_v104_persistent.cu, gemm_v105_pair.cu).
 #pragma once
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <mutex>
 
@@ -51,14 +52,17 @@ int launch_umma(const GemmProblem& p) {
   args.K = (int)p.K;
   args.tiles_m = (int)((p.M + BM_T - 1) / BM_T);
   args.tiles_n = (int)((p.N + BN - 1) / BN);
-  // M-blocks per raster group (KEBAB_GROUP_M overrides). 8 measured best at
-  // 8192^3 on B200: 1.17 GB of DRAM reads per launch against 1.31 GB at 16
-  // and 2.3 GB at 2 or 32.
+  // M-blocks per raster group (KEBAB_GROUP_M overrides). A wave of C tiles
+  // running at once streams (group) A panels and (wave / group) B panels; a B
+  // panel is BN / BM_T times an A panel, so the bytes per wave are smallest
+  // near group = sqrt(wave * BN / BM_T): 8 for 256 x 256 pair tiles, 12 for
+  // 256 x 512 (measured on B200: v105 8192^3 DRAM reads 1.17 GB at 8 vs 1.31
+  // at 16; v107 16384 x 28672 x 8192 1200 TFLOP/s at 16 vs 1142 at 8).
   static const int group_env = [] {
     const char* e = std::getenv("KEBAB_GROUP_M");
     return (e && *e) ? std::atoi(e) : 0;
   }();
-  args.group_m = group_env > 0 ? group_env : 8;
+  args.group_m = group_env;  // resolved below, once the wave size is known
   // Epilogue poll backoff in ns (KEBAB_EPI_BACKOFF_NS; default 0 = spin).
   static const uint32_t backoff_env = [] {
     const char* e = std::getenv("KEBAB_EPI_BACKOFF_NS");
@@ -113,6 +117,10 @@ int launch_umma(const GemmProblem& p) {
     clusters = (int)tiles;
   }
 
+  if (args.group_m <= 0) {
+    const double wave = PERSISTENT ? (double)clusters : (double)dev->sm_count / CG;
+    args.group_m = std::max(1, (int)std::lround(std::sqrt(wave * BN / BM_T)));
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);
   cfg.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
