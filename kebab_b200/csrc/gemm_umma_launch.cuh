@@ -55,9 +55,10 @@ int launch_umma(const GemmProblem& p) {
   // M-blocks per raster group (KEBAB_GROUP_M overrides). A wave of C tiles
   // running at once streams (group) A panels and (wave / group) B panels; a B
   // panel is BN / BM_T times an A panel, so the bytes per wave are smallest
-  // near group = sqrt(wave * BN / BM_T): 8 for 256 x 256 pair tiles, 12 for
-  // 256 x 512 (measured on B200: v105 8192^3 DRAM reads 1.17 GB at 8 vs 1.31
-  // at 16; v107 16384 x 28672 x 8192 1200 TFLOP/s at 16 vs 1142 at 8).
+  // near group = sqrt(wave * BN / BM_T): ~8.6 for 256 x 256 pair tiles, ~12
+  // for 256 x 512 (measured on B200: v105 8192^3 DRAM reads 1.17 GB at 8 vs
+  // 1.31 at 16; v107 16384 x 28672 x 8192: 1239 TFLOP/s at 16, 1186 at 12,
+  // 1152 at 8).
   static const int group_env = [] {
     const char* e = std::getenv("KEBAB_GROUP_M");
     return (e && *e) ? std::atoi(e) : 0;
@@ -118,8 +119,21 @@ int launch_umma(const GemmProblem& p) {
   }
 
   if (args.group_m <= 0) {
+    // Target group size, snapped to a divisor of tiles_m (no ragged last
+    // group, whose waves would straddle two groups); ties go to the larger.
     const double wave = PERSISTENT ? (double)clusters : (double)dev->sm_count / CG;
-    args.group_m = std::max(1, (int)std::lround(std::sqrt(wave * BN / BM_T)));
+    const double target = std::sqrt(wave * BN / BM_T);
+    int best = 1;
+    double best_err = 1e30;
+    for (int d = 1; d <= args.tiles_m; ++d) {
+      if (args.tiles_m % d) continue;
+      const double err = std::fabs(std::log((double)d / target));
+      if (err <= best_err + 1e-9) {
+        best = d;
+        best_err = err;
+      }
+    }
+    args.group_m = best;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);
