@@ -38,6 +38,8 @@ const Rung kRungs[] = {
     {105, "tma_umma_tmem_warpspecialized_persistent_2cta", launch_v105_pair},
     {106, "tma_umma_tmem_swapab_splitk_cluster_skinny", launch_v106_skinny},
     {107, "tma_umma_tmem_warpspecialized_persistent_2cta_256x512", launch_v107_pair_wide},
+    {108, "tma_umma_tmem_warpspecialized_persistent_streamk", launch_v108_streamk},
+    {109, "tma_umma_tmem_warpspecialized_persistent_2cta_streamk", launch_v109_pair_streamk},
     {141, "tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c", launch_v105_pair},
 };
 
@@ -204,6 +206,8 @@ KEBAB_RUNG_LAUNCHER(gemm_v104_tma_umma_tmem_warpspecialized_persistent, 104)
 KEBAB_RUNG_LAUNCHER(gemm_v105_tma_umma_tmem_warpspecialized_persistent_2cta, 105)
 KEBAB_RUNG_LAUNCHER(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny, 106)
 KEBAB_RUNG_LAUNCHER(gemm_v107_tma_umma_tmem_warpspecialized_persistent_2cta_256x512, 107)
+KEBAB_RUNG_LAUNCHER(gemm_v108_tma_umma_tmem_warpspecialized_persistent_streamk, 108)
+KEBAB_RUNG_LAUNCHER(gemm_v109_tma_umma_tmem_warpspecialized_persistent_2cta_streamk, 109)
 KEBAB_RUNG_LAUNCHER(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c, 141)
 #undef KEBAB_RUNG_LAUNCHER
 

@@ -68,9 +68,121 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
   nb = r / gm;
 }
 
+// One unit of work of a CTA (pair): K-blocks [k0, k1) of a tile. role:
+// 0 = the whole tile, 1 = the tile's last K-blocks (owner: adds the partials
+// of the contributors, then stores C), 2 = earlier K-blocks (contributor:
+// publishes an FP32 partial).
+struct WorkUnit {
+  int tile, k0, k1, role;
+  int first_cluster;  // owner: first contributing cluster
+};
+
+// Enumerates a cluster's units in processing order: whole tiles first (round
+// robin), then its stream-K range, contributor segment first so that owners,
+// which are processed later by other clusters, rarely wait.
+struct UnitIter {
+  int cluster, clusters, num_kb;
+  int dp_tiles, sk_tiles;
+  bool sk, persistent;
+  int num_tiles;
+  // state
+  int dp_next;
+  long long s, e;           // stream-K iteration range [s, e)
+  int seg, nseg, t_first, t_last;
+  bool contrib_first;
+
+  __device__ void init(int c, int nc, int kb, int dp, int skt, bool use_sk, bool pers, int tiles) {
+    cluster = c;
+    clusters = nc;
+    num_kb = kb;
+    dp_tiles = use_sk ? dp : tiles;
+    sk_tiles = use_sk ? skt : 0;
+    sk = use_sk;
+    persistent = pers;
+    num_tiles = tiles;
+    dp_next = c;
+    const long long S = (long long)sk_tiles * kb;
+    s = S * c / nc;
+    e = S * (c + 1) / nc;
+    seg = 0;
+    if (e > s) {
+      t_first = (int)(s / kb);
+      t_last = (int)((e - 1) / kb);
+      nseg = t_last - t_first + 1;
+      contrib_first = (e - (long long)t_last * kb) < kb;
+    } else {
+      nseg = 0;
+    }
+  }
+  // first cluster whose range contains SK iteration `it`
+  __device__ int cluster_of(long long it) const {
+    const long long S = (long long)sk_tiles * num_kb;
+    return (int)(((it + 1) * clusters + S - 1) / S) - 1;
+  }
+  __device__ bool next(WorkUnit& u) {
+    if (dp_next < dp_tiles) {
+      u.tile = dp_next;
+      u.k0 = 0;
+      u.k1 = num_kb;
+      u.role = 0;
+      u.first_cluster = cluster;
+      dp_next = persistent ? dp_next + clusters : dp_tiles;
+      return true;
+    }
+    if (seg >= nseg) return false;
+    // segment order: contributor (the last tile) first when there is one
+    int t;
+    if (contrib_first) t = (seg == 0) ? t_last : t_first + seg - 1;
+    else t = t_first + seg;
+    ++seg;
+    const long long base = (long long)t * num_kb;
+    u.tile = dp_tiles + t;
+    u.k0 = (int)((s > base) ? s - base : 0);
+    u.k1 = (int)((e < base + num_kb) ? e - base : num_kb);
+    if (u.k0 == 0 && u.k1 == num_kb) u.role = 0;
+    else if (u.k1 == num_kb) u.role = 1;
+    else u.role = 2;
+    u.first_cluster = cluster_of(base);
+    return true;
+  }
+};
+
+// Bounded wait until a flag written by another CTA equals `want`.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, const WaitCtx& ctx) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+  if (v == want) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    __nanosleep(64);
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == want) return true;
+    if ((it & 63u) == 0u) {
+      if (aborted(ctx.status)) return false;
+      if (globaltimer() - t0 > ctx.timeout_ns) {
+        record_error(ctx.status, DEV_TIMEOUT, SITE_PARTIAL);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void set_flag(uint32_t* flag, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
 struct UmmaArgs {
   int M, N, K;
   int tiles_m, tiles_n, group_m;
+  // Stream-K (SK kernels only): tiles [0, dp_tiles) are whole-tile work split
+  // round-robin; the K-iterations of tiles [dp_tiles, dp_tiles + sk_tiles)
+  // are split evenly over the clusters. Partials go to ws (one 128 x BN FP32
+  // slot per CTA) and are announced in flags (one per CTA and epilogue warp)
+  // with the value `epoch`.
+  int dp_tiles, sk_tiles;
+  uint32_t epoch;
+  float* ws;
+  uint32_t* flags;
   uint32_t epi_backoff_ns;  // sleep between polls of the epilogue's accumulator wait (0 = spin)
   int l2_hint;              // 0: no hint; bits 0..1 policy of A, bits 2..3 of B (1 last, 2 first, 3 normal)
   WaitCtx ctx;
@@ -111,7 +223,7 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
   else return umma_desc_sw128(base + k * 32);                          // 16 K elements = 32 bytes
 }
 
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0>
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0, bool SK = false>
 __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     gemm_umma_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const UmmaArgs args) {
@@ -123,6 +235,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   constexpr int NSUB = BN / 256 > 1 ? BN / 256 : 1;
   constexpr int ACCS = (2 * BN <= TMEM_COLS) ? 2 : 1;
   static_assert(BN <= 256 || (BN == 512 && CG == 2), "BN = 512 needs CTA pairs");
+  static_assert(!SK || (PERSISTENT && BN <= 256), "stream-K needs the persistent 4-warp epilogue");
   constexpr bool A_MN = (LAYOUT & LAYOUT_A_MN) != 0;
   constexpr bool B_MN = (LAYOUT & LAYOUT_B_MN) != 0;
   constexpr bool C_ROW = (LAYOUT & LAYOUT_C_ROW) != 0;
@@ -173,7 +286,6 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int cluster_id = blockIdx.x / CG;
   const int num_clusters = gridDim.x / CG;
-  const int tile_step = PERSISTENT ? num_clusters : num_tiles;  // non-persistent: exactly one tile
   const int num_kb = (args.K + L::BK - 1) / L::BK;
 
   if (warp == 0) {
@@ -186,12 +298,15 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       bool issued[STAGES];
       for (int s = 0; s < STAGES; ++s) issued[s] = false;
       const uint32_t full_leader0 = (CG == 2) ? mapa_shared(smem_u32(&full[0]), 0) : 0u;
-      for (int tile = cluster_id; ok && tile < num_tiles; tile += tile_step) {
+      UnitIter it;
+      it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
+      WorkUnit u;
+      while (ok && it.next(u)) {
         int mb, nb;
-        tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+        tile_coords(u.tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
         const int m0 = mb * BM_T + (int)rank * 128;
         const int n0 = nb * BN + (int)rank * (BN / CG);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = u.k0; kb < u.k1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, ctx, SITE_EMPTY)) {
             ok = false;
             break;
@@ -243,14 +358,17 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       bool any_issued = false;
-      for (int tile = cluster_id; ok && tile < num_tiles; tile += tile_step) {
+      UnitIter it;
+      it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
+      WorkUnit u;
+      while (ok && it.next(u)) {
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = u.k0; kb < u.k1; ++kb) {
           if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
             ok = false;
             break;
@@ -266,9 +384,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
               // Sub-MMA `sub` reads rows [128 sub, 128 sub + 128) of each CTA's B tile.
               const uint64_t bd = operand_desc<B_MN>(b_addr + sub * (128 * L::BK * 2), k);
               if constexpr (CG == 1)
-                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (kb != u.k0 || k != 0) ? 1u : 0u);
               else
-                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (kb | k) != 0 ? 1u : 0u);
+                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (kb != u.k0 || k != 0) ? 1u : 0u);
             }
           }
           any_issued = true;
@@ -306,19 +424,59 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int sub = 0;
-    for (int tile = cluster_id; tile < num_tiles; tile += tile_step) {
+    UnitIter it;
+    it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
+    WorkUnit u;
+    bool ok = true;
+    while (ok && it.next(u)) {
       int mb, nb;
-      tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
+      tile_coords(u.tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
       const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
       const int n0 = nb * BN;
       if (!mbar_wait_backoff(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL, args.epi_backoff_ns)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      // Stream-K: this thread's row of this CTA's partial slot, and (owner)
+      // the contributors, whose flags must carry this launch's epoch.
+      float* my_slot = nullptr;
+      if constexpr (SK) {
+        my_slot = args.ws + ((size_t)blockIdx.x * 128 + q * 32 + lane) * BN;
+        if (u.role == 1) {
+          for (int cc = u.first_cluster; cc < cluster_id && ok; ++cc)
+            if (lane == 0 && !wait_flag(args.flags + (size_t)(cc * CG + rank) * 4 + q, args.epoch, ctx)) ok = false;
+          ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+          __syncwarp();
+        }
+      }
 #pragma unroll 1
       for (int c = c0; c < c0 + CHUNKS; ++c) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), v);
         tmem_ld_wait();
+        if constexpr (SK) {
+          if (u.role == 2) {
+            // Contributor: publish the FP32 partial of columns [32c, 32c + 32).
+            float4* dst = reinterpret_cast<float4*>(my_slot + c * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                   __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+          } else if (u.role == 1 && ok) {
+            // Owner: add the contributors' partials in cluster order.
+            for (int cc = u.first_cluster; cc < cluster_id; ++cc) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  args.ws + ((size_t)(cc * CG + rank) * 128 + q * 32 + lane) * BN + c * 32);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 p4 = __ldcg(src + j);
+                v[4 * j] = __float_as_uint(__uint_as_float(v[4 * j]) + p4.x);
+                v[4 * j + 1] = __float_as_uint(__uint_as_float(v[4 * j + 1]) + p4.y);
+                v[4 * j + 2] = __float_as_uint(__uint_as_float(v[4 * j + 2]) + p4.z);
+                v[4 * j + 3] = __float_as_uint(__uint_as_float(v[4 * j + 3]) + p4.w);
+              }
+            }
+          }
+        }
         if (c == c0 + CHUNKS - 1) {
           // Accumulator fully read: hand it back to the MMA issuer.
           tc_fence_before();
@@ -328,6 +486,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
             else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
           }
         }
+        if (SK && u.role == 2) continue;  // a contributor stores no C
         T* buf = stage_c + (sub & 1) * (32 * 32);
         if (lane == 0) tma_store_wait_read<1>();  // the store that used `buf` has read it
         __syncwarp();
@@ -360,6 +519,14 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           tma_store_commit();
         }
         ++sub;
+      }
+      if constexpr (SK) {
+        if (u.role == 2) {
+          // Partial written: make it visible GPU-wide, then raise this warp's flag.
+          __syncwarp();
+          __threadfence();
+          if (lane == 0) set_flag(args.flags + (size_t)blockIdx.x * 4 + q, args.epoch);
+        }
       }
       if (++acc == ACCS) {
         acc = 0;

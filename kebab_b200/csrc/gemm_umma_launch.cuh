@@ -13,7 +13,7 @@
 namespace kb {
 namespace umma_launch {
 
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT>
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT, bool SK = false>
 int launch_umma(const GemmProblem& p) {
   using L = UmmaSmem<BN, STAGES, CG>;
   int rc = check_tma_shapes(p);
@@ -79,7 +79,7 @@ int launch_umma(const GemmProblem& p) {
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
 
-  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT>;
+  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>;
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
   const int di = dev->device & 63;
@@ -135,6 +135,25 @@ int launch_umma(const GemmProblem& p) {
     }
     args.group_m = best;
   }
+  // Work split: whole tiles round robin; with stream-K the last partial wave
+  // plus one full wave (or all tiles when there is less than one wave) are
+  // split by K-iterations evenly over the clusters.
+  args.dp_tiles = (int)tiles;
+  args.sk_tiles = 0;
+  args.ws = nullptr;
+  args.flags = nullptr;
+  args.epoch = 0;
+  if (SK) {
+    const long long waves = tiles / clusters, rem = tiles % clusters;
+    if (rem != 0) {
+      args.sk_tiles = (int)(waves >= 1 ? rem + clusters : rem);
+      args.dp_tiles = (int)(tiles - args.sk_tiles);
+      const size_t ctas = (size_t)CG * clusters;
+      if ((rc = sk_workspace(p.stream, ctas * 128 * BN * sizeof(float), ctas * 4, &args.ws, &args.flags,
+                             &args.epoch)))
+        return rc;
+    }
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);
   cfg.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
@@ -154,26 +173,26 @@ int launch_umma(const GemmProblem& p) {
 
 
 
-template <int CG, bool PERSISTENT, int STAGES, int LAYOUT, int BN>
+template <int CG, bool PERSISTENT, int STAGES, int LAYOUT, int BN, bool SK>
 int dispatch_dtype(const GemmProblem& p) {
-  if (p.dtype == KEBAB_F16) return launch_umma<__half, BN, STAGES, CG, PERSISTENT, LAYOUT>(p);
-  return launch_umma<__nv_bfloat16, BN, STAGES, CG, PERSISTENT, LAYOUT>(p);
+  if (p.dtype == KEBAB_F16) return launch_umma<__half, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>(p);
+  return launch_umma<__nv_bfloat16, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>(p);
 }
 
 // Layout from the problem: A column-major, B row-major, C row-major bits.
-template <int CG, bool PERSISTENT, int STAGES, int BN = 256>
+template <int CG, bool PERSISTENT, int STAGES, int BN = 256, bool SK = false>
 int dispatch(const GemmProblem& p) {
   const int layout = (p.lhs == 'C' ? LAYOUT_A_MN : 0) | (p.rhs == 'R' ? LAYOUT_B_MN : 0) |
                      (p.c_row ? LAYOUT_C_ROW : 0);
   switch (layout) {
-    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0, BN>(p);
-    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1, BN>(p);
-    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2, BN>(p);
-    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3, BN>(p);
-    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4, BN>(p);
-    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5, BN>(p);
-    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6, BN>(p);
-    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7, BN>(p);
+    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0, BN, SK>(p);
+    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1, BN, SK>(p);
+    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2, BN, SK>(p);
+    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3, BN, SK>(p);
+    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4, BN, SK>(p);
+    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5, BN, SK>(p);
+    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6, BN, SK>(p);
+    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7, BN, SK>(p);
   }
 }
 

@@ -38,6 +38,13 @@ int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, u
 int make_tmap_2d_sw(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
                     uint32_t box_rows, uint32_t box_cols, int swizzle_bytes);
 
+// Stream-K workspace of the calling (device, stream): `ws_bytes` of FP32
+// partials and `flags` uint32 flags (zeroed once, when allocated), plus the
+// epoch this launch must write into the flags (one more than the last).
+// Allocated on first use and grown as needed; freed by kebab_shutdown().
+int sk_workspace(cudaStream_t stream, size_t ws_bytes, size_t flags, float** ws, uint32_t** flag_ptr,
+                 uint32_t* epoch);
+
 // Problem description passed to every launcher.
 struct GemmProblem {
   int dtype;  // KEBAB_F16 / KEBAB_BF16
@@ -59,6 +66,8 @@ int launch_v104_persistent(const GemmProblem& p);
 int launch_v105_pair(const GemmProblem& p);
 int launch_v106_skinny(const GemmProblem& p);
 int launch_v107_pair_wide(const GemmProblem& p);
+int launch_v108_streamk(const GemmProblem& p);
+int launch_v109_pair_streamk(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and

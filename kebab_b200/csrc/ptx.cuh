@@ -29,6 +29,7 @@ enum WaitSite : uint32_t {
   SITE_TMA_DONE = 6,    // single-stage kernels waiting for their TMA
   SITE_PROBE = 7,       // the deliberate-timeout probe kernel
   SITE_DRAIN = 8,       // teardown drain after an abort
+  SITE_PARTIAL = 9,     // stream-K owner waiting for a contributor's partial
 };
 
 // Where a kernel reports a failed wait, and how long a wait may take.

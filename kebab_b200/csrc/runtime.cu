@@ -6,8 +6,10 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "internal.h"
@@ -147,6 +149,44 @@ int check_tma_shapes(const GemmProblem& p) {
   return KEBAB_OK;
 }
 
+namespace {
+struct SkWorkspace {
+  void* base = nullptr;
+  size_t ws_bytes = 0, flags = 0;
+  uint32_t epoch = 0;
+};
+std::map<std::pair<int, cudaStream_t>, SkWorkspace> g_sk;
+}  // namespace
+
+int sk_workspace(cudaStream_t stream, size_t ws_bytes, size_t flags, float** ws, uint32_t** flag_ptr,
+                 uint32_t* epoch) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_mu);
+  SkWorkspace& w = g_sk[{dev, stream}];
+  if (w.ws_bytes < ws_bytes || w.flags < flags) {
+    if (w.base) {
+      cudaStreamSynchronize(stream);
+      cudaFree(w.base);
+      w.base = nullptr;
+    }
+    const size_t ws_round = (ws_bytes + 255) & ~size_t(255);
+    if ((e = cudaMalloc(&w.base, ws_round + flags * sizeof(uint32_t))) != cudaSuccess)
+      return cuda_fail(e, "cudaMalloc(stream-K workspace)");
+    if ((e = cudaMemset(static_cast<uint8_t*>(w.base) + ws_round, 0, flags * sizeof(uint32_t))) != cudaSuccess)
+      return cuda_fail(e, "cudaMemset(stream-K flags)");
+    w.ws_bytes = ws_round;
+    w.flags = flags;
+    w.epoch = 0;
+  }
+  *ws = static_cast<float*>(w.base);
+  *flag_ptr = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(w.base) + w.ws_bytes);
+  if (++w.epoch == 0) ++w.epoch;  // 0 is the value of never-written flags
+  *epoch = w.epoch;
+  return KEBAB_OK;
+}
+
 // ---------------------------------------------------------------------------
 // Deliberate-timeout probe: one warp waits on an mbarrier that nothing will
 // ever arrive at; the bounded wait expires, records the error and returns.
@@ -217,6 +257,9 @@ int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us) {
 
 void kebab_shutdown(void) {
   std::lock_guard<std::mutex> lk(g_mu);
+  for (auto& kv : g_sk)
+    if (kv.second.base) cudaFree(kv.second.base);
+  g_sk.clear();
   for (auto* d : g_devices) delete d;
   g_devices.clear();
 }
