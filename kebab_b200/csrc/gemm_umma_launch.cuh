@@ -113,7 +113,8 @@ int launch_umma(const GemmProblem& p) {
       }
       max_clusters = std::min(max_clusters, max_active[di]);
     }
-    clusters = (int)std::min<long long>(tiles, max_clusters);
+    // Stream-K spreads K-iterations over every SM, even with fewer tiles.
+    clusters = SK ? max_clusters : (int)std::min<long long>(tiles, max_clusters);
   } else {
     clusters = (int)tiles;
   }
@@ -145,8 +146,14 @@ int launch_umma(const GemmProblem& p) {
   args.epoch = 0;
   if (SK) {
     const long long waves = tiles / clusters, rem = tiles % clusters;
-    if (rem != 0) {
-      args.sk_tiles = (int)(waves >= 1 ? rem + clusters : rem);
+    // KEBAB_SK_MODE: 0 = remainder + one full wave (default), 1 = remainder
+    // only, 2 = every tile.
+    static const int sk_mode = [] {
+      const char* e = std::getenv("KEBAB_SK_MODE");
+      return (e && *e) ? std::atoi(e) : 0;
+    }();
+    if (rem != 0 || sk_mode == 2) {
+      args.sk_tiles = (int)(sk_mode == 2 ? tiles : (waves >= 1 && sk_mode == 0) ? rem + clusters : rem);
       args.dp_tiles = (int)(tiles - args.sk_tiles);
       const size_t ctas = (size_t)CG * clusters;
       if ((rc = sk_workspace(p.stream, ctas * 128 * BN * sizeof(float), ctas * 4, &args.ws, &args.flags,
