@@ -15,7 +15,9 @@ import ctypes
 import os
 
 PKG = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(PKG, "lib", "libkebab_b200.so")
+# KEBAB_B200_LIB selects another build of the same library (e.g. an
+# instrumented one); the default is the in-tree build.
+LIB_PATH = os.environ.get("KEBAB_B200_LIB") or os.path.join(PKG, "lib", "libkebab_b200.so")
 
 F16, BF16, F32 = 0, 1, 2
 OK, EINVAL, ENOTSUP, ECUDA, ETIMEOUT, ESPARSE = 0, 22, 95, 1001, 1002, 1003

@@ -171,6 +171,14 @@ __device__ __forceinline__ void set_flag(uint32_t* flag, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
 }
 
+#ifdef KEBAB_SK_TRACE
+// Debug builds only: per-CTA event timestamps, [cta][slot][8] u64.
+__device__ unsigned long long g_sk_trace[296 * 8 * 8];
+#define SK_TRACE(slot, ev) g_sk_trace[((size_t)blockIdx.x * 8 + (slot)) * 8 + (ev)] = globaltimer()
+#else
+#define SK_TRACE(slot, ev) ((void)0)
+#endif
+
 struct UmmaArgs {
   int M, N, K;
   int tiles_m, tiles_n, group_m;
@@ -361,7 +369,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       UnitIter it;
       it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
       WorkUnit u;
+      int uidx = 0;
       while (ok && it.next(u)) {
+        SK_TRACE(uidx & 7, 0);
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
           ok = false;
           break;
@@ -398,6 +408,8 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           }
         }
         if (!ok) break;
+        SK_TRACE(uidx & 7, 1);
+        ++uidx;
         if constexpr (CG == 1) umma_commit_cg1(&tmem_full[acc]);
         else umma_commit_cg2_mc(&tmem_full[acc], 0x3);
         if (++acc == ACCS) {
@@ -428,12 +440,14 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
     WorkUnit u;
     bool ok = true;
+    int uidx = 0;
     while (ok && it.next(u)) {
       int mb, nb;
       tile_coords(u.tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
       const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
       const int n0 = nb * BN;
       if (!mbar_wait_backoff(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL, args.epi_backoff_ns)) break;
+      if (q == 0 && lane == 0) SK_TRACE(uidx & 7, 2);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       // Stream-K: this thread's row of this CTA's partial slot, and (owner)
@@ -446,6 +460,13 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
             if (lane == 0 && !wait_flag(args.flags + (size_t)(cc * CG + rank) * 4 + q, args.epoch, ctx)) ok = false;
           ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
           __syncwarp();
+        }
+        if (q == 0 && lane == 0) {
+          SK_TRACE(uidx & 7, 3);
+#ifdef KEBAB_SK_TRACE
+          g_sk_trace[((size_t)blockIdx.x * 8 + (uidx & 7)) * 8 + 5] = (unsigned long long)u.tile << 32 | (uint32_t)(u.k0 << 16 | u.k1);
+          g_sk_trace[((size_t)blockIdx.x * 8 + (uidx & 7)) * 8 + 6] = (unsigned long long)u.role << 32 | (uint32_t)u.first_cluster;
+#endif
         }
       }
 #pragma unroll 1
@@ -528,6 +549,8 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           if (lane == 0) set_flag(args.flags + (size_t)blockIdx.x * 4 + q, args.epoch);
         }
       }
+      if (q == 0 && lane == 0) SK_TRACE(uidx & 7, 4);
+      ++uidx;
       if (++acc == ACCS) {
         acc = 0;
         acc_phase ^= 1u;

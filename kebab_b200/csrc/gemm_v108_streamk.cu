@@ -11,3 +11,10 @@ namespace kb {
 int launch_v108_streamk(const GemmProblem& p) { return umma_launch::dispatch<1, true, 4, 256, true>(p); }
 
 }  // namespace kb
+
+#ifdef KEBAB_SK_TRACE
+// Debug builds only: copy this translation unit's stream-K trace to the host.
+extern "C" int kebab_debug_sk_trace_v108(void* host, size_t bytes) {
+  return (int)cudaMemcpyFromSymbol(host, kb::g_sk_trace, bytes);
+}
+#endif
