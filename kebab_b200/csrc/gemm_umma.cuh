@@ -454,7 +454,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       // the contributors, whose flags must carry this launch's epoch.
       float* my_slot = nullptr;
       if constexpr (SK) {
-        my_slot = args.ws + ((size_t)blockIdx.x * 128 + q * 32 + lane) * BN;
+        // Slot layout: [chunk][lane quarter][column][row]: for each column a
+        // warp reads or writes 32 consecutive floats (one 128-byte line).
+        my_slot = args.ws + (size_t)blockIdx.x * 128 * BN + q * 1024 + lane;
         if (u.role == 1) {
           for (int cc = u.first_cluster; cc < cluster_id && ok; ++cc)
             if (lane == 0 && !wait_flag(args.flags + (size_t)(cc * CG + rank) * 4 + q, args.epoch, ctx)) ok = false;
@@ -477,24 +479,18 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
         if constexpr (SK) {
           if (u.role == 2) {
             // Contributor: publish the FP32 partial of columns [32c, 32c + 32).
-            float4* dst = reinterpret_cast<float4*>(my_slot + c * 32);
+            float* dst = my_slot + c * 4096;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
-                                   __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            for (int j = 0; j < 32; ++j) __stcg(dst + j * 32, __uint_as_float(v[j]));
           } else if (u.role == 1 && ok) {
             // Owner: add the contributors' partials in cluster order.
             for (int cc = u.first_cluster; cc < cluster_id; ++cc) {
-              const float4* src = reinterpret_cast<const float4*>(
-                  args.ws + ((size_t)(cc * CG + rank) * 128 + q * 32 + lane) * BN + c * 32);
+              const float* src = args.ws + (size_t)(cc * CG + rank) * 128 * BN + c * 4096 + q * 1024 + lane;
+              float p[32];
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 p4 = __ldcg(src + j);
-                v[4 * j] = __float_as_uint(__uint_as_float(v[4 * j]) + p4.x);
-                v[4 * j + 1] = __float_as_uint(__uint_as_float(v[4 * j + 1]) + p4.y);
-                v[4 * j + 2] = __float_as_uint(__uint_as_float(v[4 * j + 2]) + p4.z);
-                v[4 * j + 3] = __float_as_uint(__uint_as_float(v[4 * j + 3]) + p4.w);
-              }
+              for (int j = 0; j < 32; ++j) p[j] = __ldcg(src + j * 32);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(__uint_as_float(v[j]) + p[j]);
             }
           }
         }
