@@ -89,7 +89,14 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
   // little N padding.
   if (wide_tiles >= 2 * pairs && N % 512 == 0) return 107;
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
-  if (pair_tiles >= pairs) return 105;
+  // With 1..4 full waves and a partial last one, stream-K over the last two
+  // waves wins (4096^3: 103 vs 108 us); with less than one wave every tile
+  // would be split and the partial traffic costs more than it saves.
+  if (pair_tiles >= pairs) {
+    const int64_t waves = pair_tiles / pairs, rem = pair_tiles % pairs;
+    if (rem != 0 && waves <= 4) return 109;
+    return 105;
+  }
   return 104;
 }
 

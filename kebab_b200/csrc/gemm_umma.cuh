@@ -114,6 +114,11 @@ struct UnitIter {
       nseg = 0;
     }
   }
+  // does cluster `c` have a non-empty stream-K range (and so a partial)?
+  __device__ bool has_range(int c) const {
+    const long long S = (long long)sk_tiles * num_kb;
+    return S * (c + 1) / clusters > S * c / clusters;
+  }
   // first cluster whose range contains SK iteration `it`
   __device__ int cluster_of(long long it) const {
     const long long S = (long long)sk_tiles * num_kb;
@@ -459,7 +464,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
         my_slot = args.ws + (size_t)blockIdx.x * 128 * BN + q * 1024 + lane;
         if (u.role == 1) {
           for (int cc = u.first_cluster; cc < cluster_id && ok; ++cc)
-            if (lane == 0 && !wait_flag(args.flags + (size_t)(cc * CG + rank) * 4 + q, args.epoch, ctx)) ok = false;
+            if (it.has_range(cc) && lane == 0 &&
+                !wait_flag(args.flags + (size_t)(cc * CG + rank) * 4 + q, args.epoch, ctx))
+              ok = false;
           ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
           __syncwarp();
         }
@@ -485,6 +492,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           } else if (u.role == 1 && ok) {
             // Owner: add the contributors' partials in cluster order.
             for (int cc = u.first_cluster; cc < cluster_id; ++cc) {
+              if (!it.has_range(cc)) continue;  // clusters with no K-iterations publish nothing
               const float* src = args.ws + (size_t)(cc * CG + rank) * 128 * BN + c * 4096 + q * 1024 + lane;
               float p[32];
 #pragma unroll

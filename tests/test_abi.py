@@ -88,4 +88,5 @@ def test_v120_heuristic_without_gpu():
     r_small = kb.lib().kebab_resolve_version(120, kb.F16, 1024, 256, 8192)
     r_skinny = kb.lib().kebab_resolve_version(120, kb.F16, 64, 8192, 8192)
     r_mid = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 8192)
-    assert r_big == 107 and r_mid == 105 and r_small == 104 and r_skinny == 106
+    r_mid2 = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 4096)
+    assert r_big == 107 and r_mid == 109 and r_mid2 == 109 and r_small == 104 and r_skinny == 106
