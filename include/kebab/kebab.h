@@ -90,6 +90,19 @@ int kebab_set_wait_timeout_us(uint64_t timeout_us);
  * it. */
 int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us);
 
+/* Stream-K GEMM (rung 109's kernel: CTA pairs, RC, column-major C) that
+ * allocates no device memory, for callers that cannot call cudaMalloc at that
+ * point — a custom allocator or pool callback, a serving loop with a fixed
+ * memory budget, a plugin host that forbids allocation after start-up. Its
+ * scratch is a static device array present on every GPU that loads the
+ * library: 160 partial-tile slots of 128 KiB (20 MiB) plus 2.5 KiB of flags;
+ * a device whose grid needs more than 160 CTAs gets KEBAB_ENOTSUP. The first
+ * call on a device sets up (looks up the array's address); make it before any
+ * stream capture. All calls share the array, so calls that overlap on the GPU
+ * race. No counterpart in the reference. */
+int kebab_gemm_streamk_noalloc(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N,
+                               int64_t K, kebab_stream_t stream);
+
 /* Releases cached tensor maps and per-device state. Replaces nothing: the
  * reference's function-static caches are never freed (cuda_gemm_v10_*:499). */
 void kebab_shutdown(void);
