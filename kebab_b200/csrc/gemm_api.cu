@@ -66,7 +66,8 @@ int map_reference_id(int v) {
 
 // The role of the reference's v20 heuristic (cuda_gemm.cu:25-77): choose a
 // decomposition from the tile count against the QUERIED SM count.
-// KEBAB_V120_MODE = dp | persistent | pair | wide | skinny | heuristic (default).
+// KEBAB_V120_MODE = dp | persistent | pair | wide | streamk (pairs) | streamk1
+// (1-CTA) | skinny | heuristic (default).
 int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
@@ -76,6 +77,8 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
     if (m == "PERSISTENT") return 104;
     if (m == "PAIR" || m == "2CTA") return 105;
     if (m == "WIDE" || m == "PAIRWIDE") return 107;
+    if (m == "STREAMK" || m == "PAIRSTREAMK") return 109;
+    if (m == "STREAMK1") return 108;
     if ((m == "SKINNY" || m == "SPLITK") && rc_colc) return 106;
   }
   // Decode-like shapes: too few 128-row tiles to occupy the GPU; stream B
