@@ -88,12 +88,16 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
   const int64_t wide_tiles = ((M + 255) / 256) * ((N + 511) / 512);
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
   // 256 x 512 pair tiles cut operand traffic per FLOP by a quarter (lower
-  // power, higher clock under the cap); worth it with at least two waves and
-  // little N padding.
-  if (wide_tiles >= 2 * pairs && N % 512 == 0) return 107;
+  // power, higher clock under the cap) and beat 256 x 256 tiles by ~5 % per
+  // tile; worth it with at least one full wave, no N padding and a last-wave
+  // fill within 5 points of the 256 x 256 tiling's (4096^3: 128 wide tiles on
+  // 74 pairs fill 86 % like 256 pair tiles do, and run at 1396 TFLOP/s
+  // against 1336 for rung 105 and 1321 for rung 109).
+  auto fill = [pairs](int64_t t) { return (double)t / (double)(((t + pairs - 1) / pairs) * pairs); };
+  if (N % 512 == 0 && wide_tiles >= pairs && fill(wide_tiles) >= fill(pair_tiles) - 0.05) return 107;
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
   // With 1..4 full waves and a partial last one, stream-K over the last two
-  // waves wins (4096^3: 103 vs 108 us); with less than one wave every tile
+  // waves wins (measured at 4096^3 with 256 x 256 tiles: 103 vs 108 us); with less than one wave every tile
   // would be split and the partial traffic costs more than it saves.
   if (pair_tiles >= pairs) {
     const int64_t waves = pair_tiles / pairs, rem = pair_tiles % pairs;

@@ -89,4 +89,10 @@ def test_v120_heuristic_without_gpu():
     r_skinny = kb.lib().kebab_resolve_version(120, kb.F16, 64, 8192, 8192)
     r_mid = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 8192)
     r_mid2 = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 4096)
-    assert r_big == 107 and r_mid == 109 and r_mid2 == 109 and r_small == 104 and r_skinny == 106
+    # N % 512 != 0: 240 pair tiles = 3 full waves + a partial one -> stream-K.
+    r_sk = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 3840, 4096)
+    # 160 wide tiles fill 72 % of the last wave against 86 % for 320 pair tiles.
+    r_sk2 = kb.lib().kebab_resolve_version(120, kb.F16, 2560, 8192, 4096)
+    c4a = kb.lib().kebab_resolve_version(120, kb.F16, 16384, 28672, 8192)
+    assert r_big == 107 and r_mid == 107 and r_mid2 == 107 and c4a == 107
+    assert r_sk == 109 and r_sk2 == 109 and r_small == 104 and r_skinny == 106
