@@ -102,6 +102,10 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (CG == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (args.pdl) {  // prologue overlapped the previous kernel; now it has completed
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int cluster_id = blockIdx.x / CG;
@@ -332,13 +336,16 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CG;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  args.pdl = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = args.pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tE, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_sparse launch");
   return KEBAB_OK;

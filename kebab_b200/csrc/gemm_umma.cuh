@@ -198,6 +198,7 @@ struct UmmaArgs {
   uint32_t* flags;
   uint32_t epi_backoff_ns;  // sleep between polls of the epilogue's accumulator wait (0 = spin)
   int l2_hint;              // 0: no hint; bits 0..1 policy of A, bits 2..3 of B (1 last, 2 first, 3 normal)
+  int pdl = 0;              // launched with programmatic stream serialisation
   WaitCtx ctx;
 };
 
@@ -295,6 +296,12 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   if constexpr (CG == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The prologue above overlaps the previous kernel on the stream when this
+  // grid is PDL-launched; global memory is touched only after it completed.
+  if (args.pdl) {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
 
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int cluster_id = blockIdx.x / CG;

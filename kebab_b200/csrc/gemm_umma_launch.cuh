@@ -166,13 +166,16 @@ int launch_umma(const GemmProblem& p) {
   cfg.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = p.stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = CG;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  args.pdl = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = args.pdl ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_umma_ws launch");
   return KEBAB_OK;

@@ -29,6 +29,11 @@ int device_info(DeviceInfo** out);  // for the current device
 // Wait context for kernels launched now (status word + current timeout).
 int wait_ctx(WaitCtx* out);
 
+// Whether launches that support it use programmatic dependent launch (their
+// prologue overlaps the previous kernel on the stream). On unless the
+// environment sets KEBAB_PDL=0.
+bool pdl_enabled();
+
 // 2D tensor map over a row-major [rows][cols] array of 2-byte elements
 // (cols contiguous, row pitch `ld` elements), box {box_cols, box_rows}.
 // swizzle128: 128-byte swizzle (box_cols * 2 must be 128).

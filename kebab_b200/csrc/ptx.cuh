@@ -164,6 +164,22 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   return r;
 }
 
+// Programmatic dependent launch. wait: block until the grids this launch
+// depends on have completed and their memory is visible (a no-op when the
+// launch has no such dependency). launch_dependents: allow the next
+// PDL-launched grid on the stream to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// A cluster barrier split in two: arrive early (releasing this thread's prior
+// writes, e.g. mbarrier initialisation), wait later (acquiring the peers').
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -182,6 +198,14 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// Prefetch one tensor-map box into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y)
+               : "memory");
 }
 
 // L2 eviction-priority policies for the cache-hinted loads below.

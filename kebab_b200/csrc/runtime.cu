@@ -93,6 +93,14 @@ int wait_ctx(WaitCtx* out) {
   return KEBAB_OK;
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("KEBAB_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 static int get_encoder() {
   std::lock_guard<std::mutex> lk(g_mu);
   if (g_encode) return KEBAB_OK;
