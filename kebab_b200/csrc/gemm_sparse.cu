@@ -12,10 +12,7 @@
 // the MMA lane copies E to 4 TMEM columns (tcgen05.cp) and issues four
 // 128 x BN x 32 sparse MMAs, MMA j reading metadata column j (addressed as
 // the even column 2*(j/2) plus selector j%2 in the instruction descriptor).
-//   CG=1: 128 x 128 tiles, two accumulators (epilogue overlaps the next tile).
-//   CG=2: CTA pairs, 256 x 256 tiles (cta_group::2): B traffic per CTA is the
-//         same as CG=1 while each MMA does twice the work; one accumulator
-//         (2 x 256 columns would leave no room for the metadata).
+// Tile shapes: see SparseCfg below.
 // The reference has no sparse GEMM (its 2:4 path is one mma.sp tile,
 // kebab/lib/microbench/sparse_mma.cu:347-428).
 #include <algorithm>
@@ -29,37 +26,74 @@ namespace kb {
 
 namespace {
 
-template <int STAGES>
+// Per stage (128 logical K): MT A_packed tiles of 128 x 64, B as two 64-wide
+// sub-tiles of BNC rows (this CTA's share of the tile's N), MT metadata
+// blocks; then the epilogue's C staging (two buffers of 32 x CW per warp).
+template <int STAGES, int MT, int BNC, int EPI_WARPS, int CW>
 struct SparseSmem {
-  static constexpr int A_STAGE = 128 * 64 * 2;
-  static constexpr int B_SUB = 128 * 64 * 2;
+  static constexpr int A_TILE = 128 * 64 * 2;
+  static constexpr int A_STAGE = MT * A_TILE;
+  static constexpr int B_SUB = BNC * 64 * 2;
   static constexpr int B_STAGE = 2 * B_SUB;
-  static constexpr int E_STAGE = 2048;
-  static constexpr int C_SUB = 32 * 32 * 2;
+  static constexpr int E_TILE = 2048;
+  static constexpr int E_STAGE = MT * E_TILE;
+  static constexpr int C_SUB = 32 * CW * 2;
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_STAGE;
   static constexpr int OFF_E = OFF_B + STAGES * B_STAGE;
   static constexpr int OFF_C = OFF_E + STAGES * E_STAGE;
-  static constexpr int OFF_BAR = OFF_C + 4 * 2 * C_SUB;
+  static constexpr int OFF_BAR = OFF_C + EPI_WARPS * 2 * C_SUB;
   static constexpr int NUM_BARS = 2 * STAGES + 4 + 1;
   static constexpr int BYTES = OFF_BAR + NUM_BARS * 8 + 16;
   static constexpr int ALLOC = BYTES + 1024;
+  static_assert(B_SUB % 1024 == 0, "128-byte-swizzled sub-tiles stay 1024-byte aligned");
   static_assert(ALLOC <= 232448, "shared memory budget exceeded");
 };
 
-template <typename T, int CG, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+// Tile shapes:
+//   CG=1, MT=1, BN=128: 128 x 128 tiles, two accumulators (the epilogue of a
+//       tile overlaps the next tile's MMAs).
+//   CG=2, MT=1, BN=256: CTA pairs, 256 x 256 tiles, one accumulator.
+//   CG=2, MT=2, BN=240: CTA pairs, 512 x 240 tiles: two 256-row M-tiles share
+//       every staged B tile. The sparse MMA runs at twice the dense rate, so
+//       operand delivery from L2 bounds it: per CTA and cycle a 256 x 256 pair
+//       tile needs ~96 bytes (A 32 + B 64), two M-tiles ~66 (B's share
+//       halves), against the ~55 bytes per SM and cycle L2 delivers under a
+//       dense GEMM. The two 240-column accumulators sit at TMEM columns 0 and
+//       256; metadata uses a 2-slot ring in columns 496..511.
+template <typename T, int CG, int STAGES, int MT, int BN>
+struct SparseCfg {
+  static constexpr int BNC = BN / CG;                      // B rows per CTA
+  static constexpr int EPI_WARPS = 4 * MT;                 // one warp per TMEM lane quarter and M-tile
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int CW = (BN % 32 == 0) ? 32 : 16;     // epilogue chunk (columns)
+  static constexpr int ACC_COLS = (MT == 1) ? BN : 256;    // TMEM columns per accumulator slot
+  static constexpr int ACCS = (MT == 1 && 2 * BN + 4 * STAGES <= 512) ? 2 : 1;
+  static constexpr int E_SLOTS = (MT == 1) ? STAGES : 2;  // TMEM metadata slots (MT x 4 columns each)
+  static constexpr int E_COL0 = (ACCS * MT - 1) * ACC_COLS + BN;
+  static_assert(E_COL0 + E_SLOTS * MT * 4 <= 512, "metadata columns must fit in TMEM");
+  static_assert(BN % CW == 0 && BN % 16 == 0 && BN <= 256, "tile width");
+  using L = SparseSmem<STAGES, MT, BNC, EPI_WARPS, CW>;
+};
+
+template <int CW>
+__device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[CW]) {
+  if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr, r);
+  else tmem_ld_32x32b_x16(taddr, r);
+}
+
+template <typename T, int CG, int STAGES, int MT, int BN>
+__global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
     gemm_sparse_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                        const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmC,
                        const UmmaArgs args) {
-  using L = SparseSmem<STAGES>;
-  constexpr int BN = 128 * CG;
-  constexpr int BM_T = 128 * CG;
-  constexpr int ACCS = (2 * BN + 4 * STAGES <= 512) ? 2 : 1;
-  constexpr int E_COL0 = ACCS * BN;
+  using Cfg = SparseCfg<T, CG, STAGES, MT, BN>;
+  using L = typename Cfg::L;
+  constexpr int BM_MMA = 128 * CG;        // rows of one MMA (one M-tile)
+  constexpr int BM_T = BM_MMA * MT;       // rows of a tile
+  constexpr int ACCS = Cfg::ACCS;
   constexpr int TMEM_COLS = 512;
-  static_assert(E_COL0 + 4 * STAGES <= TMEM_COLS, "metadata columns must fit in TMEM");
-  constexpr uint32_t IDESC = umma_idesc_f16_sparse(BM_T, BN, ElemTraits<T>::kBf16);
+  constexpr uint32_t IDESC = umma_idesc_f16_sparse(BM_MMA, BN, ElemTraits<T>::kBf16);
   constexpr uint32_t TX_BYTES = (L::A_STAGE + L::B_STAGE + L::E_STAGE) * CG;
 
   extern __shared__ uint8_t smem_raw[];
@@ -89,7 +123,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 4 * CG);
+      mbar_init(&tmem_empty[a], Cfg::EPI_WARPS * CG);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -121,9 +155,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
         int mb, nb;
         tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
-        const int m0 = mb * BM_T + (int)rank * 128;
-        const int n0 = nb * BN + (int)rank * 128;
-        const int e_row0 = (m0 / 128) * num_kb * 128;
+        const int n0 = nb * BN + (int)rank * Cfg::BNC;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, ctx, SITE_EMPTY)) {
             ok = false;
@@ -134,17 +166,29 @@ __global__ void __launch_bounds__(192, 1)
           uint8_t* sE = smem + L::OFF_E + stage * L::E_STAGE;
           if constexpr (CG == 1) {
             mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-            tma_load_2d(sA, &tmA, &full[stage], kb * 64, m0);
-            tma_load_2d(sB, &tmB, &full[stage], kb * 128, n0);
-            tma_load_2d(sB + L::B_SUB, &tmB, &full[stage], kb * 128 + 64, n0);
-            tma_load_2d(sE, &tmE, &full[stage], 0, e_row0 + kb * 128);
           } else {
             if (leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
+          }
+#pragma unroll
+          for (int t = 0; t < MT; ++t) {
+            const int m0 = mb * BM_T + t * BM_MMA + (int)rank * 128;
+            const int e_row = (m0 / 128) * num_kb * 128 + kb * 128;
+            if constexpr (CG == 1) {
+              tma_load_2d(sA + t * L::A_TILE, &tmA, &full[stage], kb * 64, m0);
+              tma_load_2d(sE + t * L::E_TILE, &tmE, &full[stage], 0, e_row);
+            } else {
+              const uint32_t fb = full_leader0 + stage * 8u;
+              tma_load_2d_pair(sA + t * L::A_TILE, &tmA, fb, kb * 64, m0);
+              tma_load_2d_pair(sE + t * L::E_TILE, &tmE, fb, 0, e_row);
+            }
+          }
+          if constexpr (CG == 1) {
+            tma_load_2d(sB, &tmB, &full[stage], kb * 128, n0);
+            tma_load_2d(sB + L::B_SUB, &tmB, &full[stage], kb * 128 + 64, n0);
+          } else {
             const uint32_t fb = full_leader0 + stage * 8u;
-            tma_load_2d_pair(sA, &tmA, fb, kb * 64, m0);
             tma_load_2d_pair(sB, &tmB, fb, kb * 128, n0);
             tma_load_2d_pair(sB + L::B_SUB, &tmB, fb, kb * 128 + 64, n0);
-            tma_load_2d_pair(sE, &tmE, fb, 0, e_row0 + kb * 128);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -159,6 +203,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t e_slot = 0;
       bool ok = true, any = false;
       for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
@@ -166,7 +211,6 @@ __global__ void __launch_bounds__(192, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
             ok = false;
@@ -176,17 +220,26 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t a_addr = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
           const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
           const uint32_t e_addr = smem_u32(smem + L::OFF_E + stage * L::E_STAGE);
-          const uint32_t e_tmem = tmem_base + (uint32_t)(E_COL0 + stage * 4);
-          // 128 rows x 16 bytes, 8-row core matrices 128 bytes apart, no swizzle.
-          tmem_cp_128x128b<CG>(e_tmem, umma_desc(e_addr, 16, 128, 0));
+          // Metadata slot: one per stage (MT = 1), or a 2-slot ring (MT = 2):
+          // tcgen05.cp and tcgen05.mma issued by this thread execute in order,
+          // so the copy into a slot follows the MMAs that read it before.
+          const uint32_t slot = (MT == 1) ? (uint32_t)stage : e_slot;
+          e_slot ^= 1u;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint64_t ad = umma_desc_sw128(a_addr + j * 32);
-            const uint64_t bd = umma_desc_sw128(b_addr + (j >> 1) * L::B_SUB + (j & 1) * 64);
-            // The metadata address must be 2-column aligned; the odd column of
-            // a pair is chosen with the descriptor's selector (bits 0..1).
-            umma_f16_sp<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)(j & ~1), IDESC | (uint32_t)(j & 1),
-                            (kb | j) != 0 ? 1u : 0u);
+          for (int t = 0; t < MT; ++t) {
+            const uint32_t d_tmem = tmem_base + (uint32_t)((acc * MT + t) * Cfg::ACC_COLS);
+            const uint32_t e_tmem = tmem_base + (uint32_t)(Cfg::E_COL0 + (slot * MT + t) * 4);
+            // 128 rows x 16 bytes, 8-row core matrices 128 bytes apart, no swizzle.
+            tmem_cp_128x128b<CG>(e_tmem, umma_desc(e_addr + t * L::E_TILE, 16, 128, 0));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint64_t ad = umma_desc_sw128(a_addr + t * L::A_TILE + j * 32);
+              const uint64_t bd = umma_desc_sw128(b_addr + (j >> 1) * L::B_SUB + (j & 1) * 64);
+              // The metadata address must be 2-column aligned; the odd column
+              // of a pair is chosen with the descriptor's selector (bits 0..1).
+              umma_f16_sp<CG>(d_tmem, ad, bd, e_tmem + (uint32_t)(j & ~1), IDESC | (uint32_t)(j & 1),
+                              (kb | j) != 0 ? 1u : 0u);
+            }
           }
           any = true;
           if constexpr (CG == 1) umma_commit_cg1(&empty[stage]);
@@ -212,8 +265,10 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else {
-    const int q = warp & 3;
-    const int ew = warp - 2;
+    constexpr int CW = Cfg::CW;
+    const int q = warp & 3;              // TMEM lane quarter
+    const int ew = warp - 2;             // epilogue warp index
+    const int t = ew >> 2;               // M-tile drained by this warp
     T* stage_c = reinterpret_cast<T*>(smem + L::OFF_C + ew * 2 * L::C_SUB);
     const uint32_t tmem_empty_leader0 = (CG == 2) ? mapa_shared(smem_u32(&tmem_empty[0]), 0) : 0u;
     int acc = 0;
@@ -222,17 +277,22 @@ __global__ void __launch_bounds__(192, 1)
     for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
       int mb, nb;
       tile_coords(tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
-      const int m_rows = mb * BM_T + (int)rank * 128 + q * 32;
+      const int m_rows = mb * BM_T + t * BM_MMA + (int)rank * 128 + q * 32;
       const int n0 = nb * BN;
       if (!mbar_wait(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((acc * MT + t) * Cfg::ACC_COLS);
+      // TMEM loads run one chunk ahead of the conversion and store.
+      constexpr int NC = BN / CW;
+      uint32_t v[CW], vn[CW];
+      tmem_ld_chunk<CW>(t_row, v);
+      tmem_ld_wait();
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), v);
-        tmem_ld_wait();
-        if (c == BN / 32 - 1) {
+      for (int c = 0; c < NC; ++c) {
+        if (c + 1 < NC) {
+          tmem_ld_chunk<CW>(t_row + (uint32_t)((c + 1) * CW), vn);
+        } else {
+          // Every column of the accumulator is in registers: release it.
           tc_fence_before();
           __syncwarp();
           if (lane == 0) {
@@ -240,18 +300,23 @@ __global__ void __launch_bounds__(192, 1)
             else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
           }
         }
-        T* buf = stage_c + (sub & 1) * (32 * 32);
+        T* buf = stage_c + (sub & 1) * (32 * CW);
         if (lane == 0) tma_store_wait_read<1>();
         __syncwarp();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+        for (int j = 0; j < CW; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, buf, m_rows, n0 + c * 32);
+          tma_store_2d(&tmC, buf, m_rows, n0 + c * CW);
           tma_store_commit();
         }
         ++sub;
+        if (c + 1 < NC) {
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < CW; ++j) v[j] = vn[j];
+        }
       }
       if (++acc == ACCS) {
         acc = 0;
@@ -277,10 +342,11 @@ int make_tmap_e(CUtensorMap* out, const void* E, int64_t M, int64_t K) {
   return make_tmap_2d(out, E, KEBAB_F16, rows, 8, 8, 128, 8, false);
 }
 
-template <typename T, int CG, int STAGES>
+template <typename T, int CG, int STAGES, int MT, int BN>
 int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                   cudaStream_t stream) {
-  using L = SparseSmem<STAGES>;
+  using Cfg = SparseCfg<T, CG, STAGES, MT, BN>;
+  using L = typename Cfg::L;
   DeviceInfo* dev = nullptr;
   int rc = device_info(&dev);
   if (rc) return rc;
@@ -288,10 +354,10 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   if ((rc = wait_ctx(&args.ctx))) return rc;
   CUtensorMap tA, tB, tE, tC;
   if ((rc = make_tmap_2d(&tA, Ap, dtype, M, K / 2, K / 2, 128, 64, true))) return rc;
-  if ((rc = make_tmap_2d(&tB, B, dtype, N, K, K, 128, 64, true))) return rc;
+  if ((rc = make_tmap_2d(&tB, B, dtype, N, K, K, Cfg::BNC, 64, true))) return rc;
   if ((rc = make_tmap_e(&tE, E, M, K))) return rc;
-  if ((rc = make_tmap_2d(&tC, C, dtype, N, M, M, 32, 32, false))) return rc;
-  constexpr int BM_T = 128 * CG, BN = 128 * CG;
+  if ((rc = make_tmap_2d(&tC, C, dtype, N, M, M, Cfg::CW, 32, false))) return rc;
+  constexpr int BM_T = 128 * CG * MT;
   args.M = (int)M;
   args.N = (int)N;
   args.K = (int)K;
@@ -300,7 +366,7 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   args.group_m = 8;
   args.epi_backoff_ns = 0;
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
-  auto kern = gemm_sparse_kernel<T, CG, STAGES>;
+  auto kern = gemm_sparse_kernel<T, CG, STAGES, MT, BN>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   const int di = dev->device & 63;
@@ -314,7 +380,7 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
     if (max_active[di] == 0) {
       cudaLaunchConfig_t qc = {};
       qc.gridDim = dim3(CG * max_clusters, 1, 1);
-      qc.blockDim = dim3(192, 1, 1);
+      qc.blockDim = dim3(Cfg::THREADS, 1, 1);
       qc.dynamicSmemBytes = L::ALLOC;
       cudaLaunchAttribute qa[1];
       qa[0].id = cudaLaunchAttributeClusterDimension;
@@ -333,7 +399,7 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   const int clusters = (int)std::min<long long>(tiles, max_clusters);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);
-  cfg.blockDim = dim3(192, 1, 1);
+  cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -349,6 +415,39 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tE, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_sparse launch");
   return KEBAB_OK;
+}
+
+// Width of the 512-row pair tiles: the candidate whose tiles fill the last
+// wave of pairs best, N padding counted; ties go to the wider tile. For
+// 8192^3, 224 gives 37 x 16 = 592 tiles = 8 full waves of 74 pairs, where 240
+// gives 35 x 16 = 560 (7.6 waves) and pads N by 2.5 %.
+int sparse_tile_n(int64_t M, int64_t N, int pairs) {
+  static const int cand[] = {240, 224, 192, 160};
+  int best = 240;
+  double best_eff = -1.0;
+  const int64_t tiles_m = (M + 511) / 512;
+  for (int bn : cand) {
+    const int64_t tiles = tiles_m * ((N + bn - 1) / bn);
+    const int64_t slots = ((tiles + pairs - 1) / pairs) * pairs;
+    const double eff = (double)(M * N) / ((double)slots * 512.0 * bn);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <typename T>
+int launch_wide(int bn, int dtype, const void* Ap, const void* E, const void* B, void* C, int64_t M, int64_t N,
+                int64_t K, cudaStream_t s) {
+  switch (bn) {
+    case 240: return launch_sparse<T, 2, 3, 2, 240>(dtype, Ap, E, B, C, M, N, K, s);
+    case 224: return launch_sparse<T, 2, 3, 2, 224>(dtype, Ap, E, B, C, M, N, K, s);
+    case 192: return launch_sparse<T, 2, 3, 2, 192>(dtype, Ap, E, B, C, M, N, K, s);
+    case 160: return launch_sparse<T, 2, 3, 2, 160>(dtype, Ap, E, B, C, M, N, K, s);
+    default: return fail(KEBAB_EINVAL, "2:4 GEMM tile width must be 240, 224, 192 or 160");
+  }
 }
 
 }  // namespace
@@ -367,12 +466,24 @@ extern "C" int kebab_gemm_sparse24(kebab_dtype dtype, const void* A_packed, cons
        reinterpret_cast<uintptr_t>(C)) & 15u)
     return fail(KEBAB_EINVAL, "2:4 GEMM buffers must be 16-byte aligned");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  // KEBAB_SPARSE_CG=1 forces 128 x 128 single-CTA tiles (default: CTA pairs).
+  // Tile shape: KEBAB_SPARSE_CG=1 forces 128 x 128 single-CTA tiles, =2 the
+  // 256 x 256 CTA-pair tiles; the default is the pair with two M-tiles
+  // (512 x BN), BN chosen by sparse_tile_n (KEBAB_SPARSE_BN overrides).
   const char* env = std::getenv("KEBAB_SPARSE_CG");
-  const bool one = env && env[0] == '1';
-  if (dtype == KEBAB_F16)
-    return one ? launch_sparse<__half, 1, 4>(dtype, A_packed, E, B, C, M, N, K, s)
-               : launch_sparse<__half, 2, 4>(dtype, A_packed, E, B, C, M, N, K, s);
-  return one ? launch_sparse<__nv_bfloat16, 1, 4>(dtype, A_packed, E, B, C, M, N, K, s)
-             : launch_sparse<__nv_bfloat16, 2, 4>(dtype, A_packed, E, B, C, M, N, K, s);
+  const int mode = (env && *env) ? std::atoi(env) : 3;
+  if (mode == 1 || mode == 2) {
+    if (dtype == KEBAB_F16)
+      return mode == 1 ? launch_sparse<__half, 1, 4, 1, 128>(dtype, A_packed, E, B, C, M, N, K, s)
+                       : launch_sparse<__half, 2, 4, 1, 256>(dtype, A_packed, E, B, C, M, N, K, s);
+    return mode == 1 ? launch_sparse<__nv_bfloat16, 1, 4, 1, 128>(dtype, A_packed, E, B, C, M, N, K, s)
+                     : launch_sparse<__nv_bfloat16, 2, 4, 1, 256>(dtype, A_packed, E, B, C, M, N, K, s);
+  }
+  DeviceInfo* dev = nullptr;
+  const int rc = device_info(&dev);
+  if (rc) return rc;
+  const char* be = std::getenv("KEBAB_SPARSE_BN");
+  const int bn = (be && *be) ? std::atoi(be) : sparse_tile_n(M, N, dev->sm_count / 2);
+  return dtype == KEBAB_F16 ? launch_wide<__half>(bn, dtype, A_packed, E, B, C, M, N, K, s)
+                            : launch_wide<__nv_bfloat16>(bn, dtype, A_packed, E, B, C, M, N, K, s);
 }
+

@@ -110,15 +110,23 @@ def _sparse_case(cuda, M, N, K, dtype, cg, monkeypatch, seed=0):
     assert_close(C.float().cpu().numpy().reshape(-1), ref, "sparse cg%d %dx%dx%d" % (cg, M, N, K), dtype)
 
 
-@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("cg", [1, 2, 3])
 @pytest.mark.parametrize("shape", [(128, 128, 128), (256, 256, 256), (384, 520, 640), (1024, 1024, 2048)])
 def test_gemm_sparse24(cuda, cg, shape, monkeypatch):
     _sparse_case(cuda, *shape, O.F16, cg, monkeypatch)
 
 
-@pytest.mark.parametrize("cg", [1, 2])
+@pytest.mark.parametrize("cg", [1, 2, 3])
 def test_gemm_sparse24_bf16(cuda, cg, monkeypatch):
     _sparse_case(cuda, 512, 512, 1024, O.BF16, cg, monkeypatch, seed=2)
+
+
+@pytest.mark.parametrize("bn", [240, 224, 192, 160])
+def test_gemm_sparse24_tile_widths(cuda, bn, monkeypatch):
+    """Every width of the 512-row pair tile, on a shape that leaves a ragged
+    last tile in both M and N."""
+    monkeypatch.setenv("KEBAB_SPARSE_BN", str(bn))
+    _sparse_case(cuda, 640, 1000, 512, O.F16, 3, monkeypatch, seed=5)
 
 
 def _host_e(meta, M, K, mode, lanes):
