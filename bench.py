@@ -275,7 +275,8 @@ def main():
     version = args.version
     resolved = kb.lib().kebab_resolve_version(version, kb.F16 if args.dtype == "fp16" else kb.BF16, M, N, K)
     if args.workload == "sparse24":
-        resolved = "sparse24_cta_pair" if os.environ.get("KEBAB_SPARSE_CG", "2") != "1" else "sparse24_1cta"
+        tm, tn = kb.sparse24_tile(M, N)
+        resolved = "sparse24_%s_%dx%d" % ("1cta" if tm == 128 else "cta_pair", tm, tn)
     sparse = args.workload == "sparse24"
     workload = "%s_rc_%s_%dx%dx%d_msharded%s" % ("gemm_sparse24" if sparse else "gemm", args.dtype,
                                                   M_global if args.strong else M, N, K,

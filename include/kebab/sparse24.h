@@ -68,6 +68,12 @@ int kebab_sparse24_compress(kebab_dtype dtype, const void* A_pruned, void* A_pac
 int kebab_gemm_sparse24(kebab_dtype dtype, const void* A_packed, const void* E, const void* B, void* C, int64_t M,
                         int64_t N, int64_t K, kebab_stream_t stream);
 
+/* Tile of the CTA-pair kernel kebab_gemm_sparse24 launches for an M x N
+ * output on the current device: writes its rows (512, or 256 / 128 when
+ * KEBAB_SPARSE_CG selects the older tiles) and columns. Returns KEBAB_OK or
+ * a KEBAB_* code. No reference counterpart. */
+int kebab_sparse24_tile(int64_t M, int64_t N, int* tile_m, int* tile_n);
+
 #ifdef __cplusplus
 }
 #endif

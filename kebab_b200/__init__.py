@@ -172,6 +172,7 @@ def _sp():
                                         c.c_void_p],
             "kebab_gemm_sparse24": [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64,
                                     c.c_int64, c.c_void_p],
+            "kebab_sparse24_tile": [c.c_int64, c.c_int64, c.POINTER(c.c_int), c.POINTER(c.c_int)],
         }.items():
             f = getattr(L, name)
             f.argtypes = args
@@ -239,6 +240,14 @@ def sparse24_compress(A_pruned, stream=None):
     check(_sp().kebab_sparse24_compress(_dtype_code(A_pruned), A_pruned.data_ptr(), packed.data_ptr(), E.data_ptr(),
                                         M, K, _stream_ptr(stream)))
     return packed, E
+
+
+def sparse24_tile(M, N):
+    """(rows, columns) of the tile kebab_gemm_sparse24 uses for an M x N output."""
+    import ctypes as c
+    tm, tn = c.c_int(), c.c_int()
+    check(_sp().kebab_sparse24_tile(M, N, c.byref(tm), c.byref(tn)))
+    return tm.value, tn.value
 
 
 def gemm_sparse24(A_packed, E, B, C=None, stream=None):

@@ -487,3 +487,20 @@ extern "C" int kebab_gemm_sparse24(kebab_dtype dtype, const void* A_packed, cons
                             : launch_wide<__nv_bfloat16>(bn, dtype, A_packed, E, B, C, M, N, K, s);
 }
 
+extern "C" int kebab_sparse24_tile(int64_t M, int64_t N, int* tile_m, int* tile_n) {
+  if (!tile_m || !tile_n) return fail(KEBAB_EINVAL, "null pointer passed to kebab_sparse24_tile");
+  if (M <= 0 || N <= 0) return fail(KEBAB_EINVAL, "invalid dimensions");
+  const char* env = std::getenv("KEBAB_SPARSE_CG");
+  const int mode = (env && *env) ? std::atoi(env) : 3;
+  if (mode == 1 || mode == 2) {
+    *tile_m = *tile_n = 128 * mode;
+    return KEBAB_OK;
+  }
+  DeviceInfo* dev = nullptr;
+  const int rc = device_info(&dev);
+  const int pairs = rc == KEBAB_OK ? dev->sm_count / 2 : 74;
+  const char* be = std::getenv("KEBAB_SPARSE_BN");
+  *tile_m = 512;
+  *tile_n = (be && *be) ? std::atoi(be) : sparse_tile_n(M, N, pairs);
+  return KEBAB_OK;
+}

@@ -122,7 +122,11 @@ def short_kernel_name(name: str, width: int = 90) -> str:
             break
     if cut is not None:
         n = n[:cut]
+    # Anonymous namespaces, as ncu prints them ("<unnamed>::", and a
+    # truncated "unnamed>::" for nested ones).
     n = n.replace("(anonymous namespace)::", "").replace("<unnamed>::", "")
+    if n.startswith("unnamed>::"):
+        n = n[len("unnamed>::"):]
     return n if len(n) <= width else n[: width - 1] + "…"
 
 

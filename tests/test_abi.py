@@ -96,3 +96,13 @@ def test_v120_heuristic_without_gpu():
     c4a = kb.lib().kebab_resolve_version(120, kb.F16, 16384, 28672, 8192)
     assert r_big == 107 and r_mid == 107 and r_mid2 == 107 and c4a == 107
     assert r_sk == 109 and r_sk2 == 109 and r_small == 104 and r_skinny == 106
+
+
+def test_sparse24_tile_choice_without_gpu(monkeypatch):
+    # 148 SMs assumed when no device can be queried: 74 pairs.
+    assert kb.sparse24_tile(8192, 8192) == (512, 224)  # 16 x 37 = 592 tiles = 8 waves
+    assert kb.sparse24_tile(4096, 4096) == (512, 240)  # 8 x 18 = 144 tiles, 97 % of 2 waves
+    monkeypatch.setenv("KEBAB_SPARSE_BN", "160")
+    assert kb.sparse24_tile(8192, 8192) == (512, 160)
+    monkeypatch.setenv("KEBAB_SPARSE_CG", "2")
+    assert kb.sparse24_tile(8192, 8192) == (256, 256)
