@@ -124,7 +124,7 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.thread.join(timeout=2)
-        sms, maxes, reasons = [], [], set()
+        sms, maxes, watts, reasons = [], [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [x.strip() for x in ln.split(",")]
@@ -135,13 +135,20 @@ class ClockSampler:
                 maxes.append(float(parts[2]))
             except ValueError:
                 continue
+            try:
+                watts.append(float(parts[3].split()[0]))
+            except (ValueError, IndexError):
+                pass
             for nm, v in zip(names, parts[5:9]):
                 if v.lower() == "active":
                     reasons.add(nm)
         if not sms:
             return None
-        return {"sm_mhz": float(np.median(sms)), "sm_max_mhz": float(max(maxes)), "reasons": sorted(reasons),
-                "samples": len(sms)}
+        out = {"sm_mhz": float(np.median(sms)), "sm_max_mhz": float(max(maxes)), "reasons": sorted(reasons),
+               "samples": len(sms)}
+        if watts:
+            out["power_w"] = float(np.median(watts))
+        return out
 
 
 def cpu_threads():
