@@ -76,6 +76,14 @@ struct SparseCfg {
   using L = SparseSmem<STAGES, MT, BNC, EPI_WARPS, CW>;
 };
 
+#ifdef KEBAB_SK_TRACE
+// Debug builds only: per CTA, per tile slot (first 8 tiles), 8 timestamps.
+__device__ unsigned long long g_sp_trace[296 * 8 * 8];
+#define SP_TRACE(slot, ev) g_sp_trace[((size_t)blockIdx.x * 8 + (slot)) * 8 + (ev)] = globaltimer()
+#else
+#define SP_TRACE(slot, ev) ((void)0)
+#endif
+
 template <int CW>
 __device__ __forceinline__ void tmem_ld_chunk(uint32_t taddr, uint32_t (&r)[CW]) {
   if constexpr (CW == 32) tmem_ld_32x32b_x32(taddr, r);
@@ -206,16 +214,20 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
       uint32_t e_slot = 0;
       bool ok = true, any = false;
       for (int tile = cluster_id; ok && tile < num_tiles; tile += num_clusters) {
+        const int tslot = (tile - cluster_id) / num_clusters;
+        if (tslot < 8) SP_TRACE(tslot, 0);
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1u, ctx, SITE_TMEM_EMPTY)) {
           ok = false;
           break;
         }
+        if (tslot < 8) SP_TRACE(tslot, 1);
         tc_fence_after();
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
             ok = false;
             break;
           }
+          if (kb == 0 && tslot < 8) SP_TRACE(tslot, 2);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
           const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
@@ -250,6 +262,7 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
           }
         }
         if (!ok) break;
+        if (tslot < 8) SP_TRACE(tslot, 3);
         if constexpr (CG == 1) umma_commit_cg1(&tmem_full[acc]);
         else umma_commit_cg2_mc(&tmem_full[acc], 0x3);
         if (++acc == ACCS) {
@@ -265,7 +278,14 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
       }
     }
   } else {
+    // Epilogue. The whole accumulator slice of this warp (32 rows x BN
+    // columns) is read from TMEM into registers, rounded to the output type
+    // and packed two per register, and TMEM is released before any store:
+    // every pair finishes a tile at about the same time, and the burst of C
+    // stores that follows is paced by L2 / DRAM write bandwidth. Stores then
+    // drain from registers while the next tile's MMAs run.
     constexpr int CW = Cfg::CW;
+    constexpr int NC = BN / CW;
     const int q = warp & 3;              // TMEM lane quarter
     const int ew = warp - 2;             // epilogue warp index
     const int t = ew >> 2;               // M-tile drained by this warp
@@ -280,31 +300,49 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
       const int m_rows = mb * BM_T + t * BM_MMA + (int)rank * 128 + q * 32;
       const int n0 = nb * BN;
       if (!mbar_wait(&tmem_full[acc], acc_phase, ctx, SITE_TMEM_FULL)) break;
+      const int tslot = (tile - cluster_id) / num_clusters;
+      if (ew == 0 && lane == 0 && tslot < 8) SP_TRACE(tslot, 4);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)((acc * MT + t) * Cfg::ACC_COLS);
-      // TMEM loads run one chunk ahead of the conversion and store.
-      constexpr int NC = BN / CW;
-      uint32_t v[CW], vn[CW];
-      tmem_ld_chunk<CW>(t_row, v);
-      tmem_ld_wait();
-#pragma unroll 1
-      for (int c = 0; c < NC; ++c) {
-        if (c + 1 < NC) {
-          tmem_ld_chunk<CW>(t_row + (uint32_t)((c + 1) * CW), vn);
-        } else {
-          // Every column of the accumulator is in registers: release it.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) {
-            if constexpr (CG == 1) mbar_arrive(&tmem_empty[acc]);
-            else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
+      // Loads in 16-column chunks, one chunk ahead of the packing.
+      constexpr int NL = BN / 16;
+      uint32_t packed[BN / 2];
+      {
+        uint32_t v[16], vn[16];
+        tmem_ld_chunk<16>(t_row, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < NL; ++c) {
+          if (c + 1 < NL) tmem_ld_chunk<16>(t_row + (uint32_t)((c + 1) * 16), vn);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            packed[c * 8 + j] = pack2(T(), __uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          if (c + 1 < NL) {
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = vn[j];
           }
         }
+      }
+      // The accumulator is in registers: release it to the MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (ew == 0 && lane == 0 && tslot < 8) SP_TRACE(tslot, 5);
+      if (lane == 0) {
+        if constexpr (CG == 1) mbar_arrive(&tmem_empty[acc]);
+        else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
+      }
+#pragma unroll
+      for (int c = 0; c < NC; ++c) {
         T* buf = stage_c + (sub & 1) * (32 * CW);
         if (lane == 0) tma_store_wait_read<1>();
         __syncwarp();
+        uint16_t* b16 = reinterpret_cast<uint16_t*>(buf);
 #pragma unroll
-        for (int j = 0; j < CW; ++j) buf[j * 32 + lane] = ElemTraits<T>::cvt(__uint_as_float(v[j]));
+        for (int j = 0; j < CW / 2; ++j) {
+          b16[(2 * j) * 32 + lane] = (uint16_t)(packed[c * (CW / 2) + j] & 0xFFFFu);
+          b16[(2 * j + 1) * 32 + lane] = (uint16_t)(packed[c * (CW / 2) + j] >> 16);
+        }
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -312,12 +350,8 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
           tma_store_commit();
         }
         ++sub;
-        if (c + 1 < NC) {
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < CW; ++j) v[j] = vn[j];
-        }
       }
+      if (ew == 0 && lane == 0 && tslot < 8) SP_TRACE(tslot, 6);
       if (++acc == ACCS) {
         acc = 0;
         acc_phase ^= 1u;
@@ -504,3 +538,9 @@ extern "C" int kebab_sparse24_tile(int64_t M, int64_t N, int* tile_m, int* tile_
   *tile_n = (be && *be) ? std::atoi(be) : sparse_tile_n(M, N, pairs);
   return KEBAB_OK;
 }
+
+#ifdef KEBAB_SK_TRACE
+extern "C" int kebab_debug_sparse_trace(void* host, size_t bytes) {
+  return (int)cudaMemcpyFromSymbol(host, kb::g_sp_trace, bytes);
+}
+#endif

@@ -55,6 +55,16 @@ struct ElemTraits<__nv_bfloat16> {
   __device__ static __forceinline__ __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
 };
 
+// Two floats rounded to the output type, packed low column first.
+__device__ __forceinline__ uint32_t pack2(__half, float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(__nv_bfloat16, float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // Grouped rasterisation: consecutive tile ids walk down `group_m` M-blocks
 // before moving to the next N-block, so concurrently running CTAs share A
 // rows and B columns in L2.
@@ -485,6 +495,53 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
 #endif
         }
       }
+      if constexpr (ACCS == 1 && !SK && !C_ROW) {
+        // Single accumulator: every pair finishes its tile at about the same
+        // time and the C stores that follow are paced by L2 / DRAM write
+        // bandwidth, so read this warp's whole slice out of TMEM first (FP16 /
+        // BF16 pairs, CHUNKS x 16 registers), hand TMEM back to the MMA
+        // issuer, and store while the next tile's MMAs run.
+        uint32_t packed[CHUNKS][16];
+#pragma unroll
+        for (int l = 0; l < 2 * CHUNKS; ++l) {
+          // 16-column loads (registers stay below the spill line with the
+          // whole slice held packed).
+          uint32_t v[16];
+          tmem_ld_32x32b_x16(t_row + (uint32_t)(c0 * 32 + l * 16), v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            packed[l >> 1][(l & 1) * 8 + j] = pack2(T(), __uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 1) mbar_arrive(&tmem_empty[acc]);
+          else mbar_arrive_cluster(tmem_empty_leader0 + (uint32_t)acc * 8u);
+        }
+#pragma unroll
+        for (int i = 0; i < CHUNKS; ++i) {
+          const int c = c0 + i;
+          T* buf = stage_c + (sub & 1) * (32 * 32);
+          if (lane == 0) tma_store_wait_read<1>();
+          __syncwarp();
+          uint16_t* b16 = reinterpret_cast<uint16_t*>(buf);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            b16[(2 * j) * 32 + lane] = (uint16_t)(packed[i][j] & 0xFFFFu);
+            b16[(2 * j + 1) * 32 + lane] = (uint16_t)(packed[i][j] >> 16);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int d = c * 32;
+            const int gcol = NSUB == 1 ? n0 + d : n0 + ((d & 255) >= 128 ? 256 : 0) + 128 * (d >> 8) + (d & 127);
+            tma_store_2d(&tmC, buf, m_rows, gcol);
+            tma_store_commit();
+          }
+          ++sub;
+        }
+      } else {
 #pragma unroll 1
       for (int c = c0; c < c0 + CHUNKS; ++c) {
         uint32_t v[32];
@@ -552,6 +609,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
         }
         ++sub;
       }
+      }  // single-accumulator path / chunked path
       if constexpr (SK) {
         if (u.role == 2) {
           // Partial written: make it visible GPU-wide, then raise this warp's flag.

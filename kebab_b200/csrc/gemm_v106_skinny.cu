@@ -72,16 +72,6 @@ __device__ unsigned long long g_skinny_trace[1024 * 32];
 #define SKY_TRACE(ev) ((void)0)
 #endif
 
-// Two floats rounded to the output type and packed low-address first.
-__device__ __forceinline__ uint32_t pack2(__half, float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ uint32_t pack2(__nv_bfloat16, float a, float b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-
 // 16 bytes into a peer's shared memory; the bytes count towards the peer's
 // mbarrier transaction (both given as shared::cluster addresses).
 __device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t bar, const uint32_t* v) {
