@@ -28,6 +28,7 @@
 #include <sstream>
 #include <string>
 #include <sys/stat.h>
+#include <type_traits>
 #include <vector>
 
 #include "config_parser.h"
@@ -114,7 +115,13 @@ int bench_precision(const ConfigParser& cfg, const std::string& out_dir) {
       const double cublas_tflops = flops / (cublas_ms * 1e-3) / 1e12;
       std::vector<T> ref = dRef.download();
       std::cout << "  " << M << "x" << N << "x" << K << " " << mode << "  cuBLAS " << std::fixed
-                << std::setprecision(1) << cublas_tflops << " TFLOP/s" << std::endl;
+                << std::setprecision(1) << cublas_tflops << " TFLOP/s (FP32 accumulate)";
+      if constexpr (std::is_same<T, __half>::value) {
+        DeviceBuffer<T> dH(M * N);
+        const float h_ms = timer.measure([&] { cublas_hgemm(handle, lhs, rhs, dA.p, dB.p, dH.p, M, N, K); });
+        std::cout << ", cublasHgemm " << flops / (h_ms * 1e-3) / 1e12 << " TFLOP/s (FP16 accumulate, the reference's)";
+      }
+      std::cout << std::endl;
       for (const auto& impl : impls) {
         if (impl != "cuda") {
           std::cout << "    impl " << impl << ": skipped (only the cuda ladder is built for sm_100a)" << std::endl;

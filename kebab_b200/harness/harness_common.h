@@ -177,6 +177,19 @@ void cublas_gemm(cublasHandle_t h, char lhs, char rhs, const T* A, const T* B, T
                             CUBLAS_GEMM_DEFAULT));
 }
 
+// The reference's own half comparator (cublas_reference.h:136): cublasHgemm,
+// FP16 accumulation. Reported beside the FP32-accumulate one above, which is
+// the fair comparator for this library's FP32-accumulate kernels.
+inline void cublas_hgemm(cublasHandle_t h, char lhs, char rhs, const __half* A, const __half* B, __half* C,
+                         long long M, long long N, long long K) {
+  const __half one = __float2half(1.0f), zero = __float2half(0.0f);
+  cublasOperation_t opA = (lhs == 'R') ? CUBLAS_OP_T : CUBLAS_OP_N;
+  cublasOperation_t opB = (rhs == 'R') ? CUBLAS_OP_T : CUBLAS_OP_N;
+  long long lda = (lhs == 'R') ? K : M;
+  long long ldb = (rhs == 'R') ? N : K;
+  CHECK_CUBLAS(cublasHgemm(h, opA, opB, (int)M, (int)N, (int)K, &one, A, (int)lda, B, (int)ldb, &zero, C, (int)M));
+}
+
 struct Check {
   bool ok;
   double rel_fro, worst;
