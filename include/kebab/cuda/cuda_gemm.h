@@ -45,6 +45,8 @@ KEBAB_DECLARE_RUNG(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny)      //
 KEBAB_DECLARE_RUNG(gemm_v107_tma_umma_tmem_warpspecialized_persistent_2cta_256x512)  // pairs, 256 x 512 tiles
 KEBAB_DECLARE_RUNG(gemm_v108_tma_umma_tmem_warpspecialized_persistent_streamk)  // v104 + stream-K
 KEBAB_DECLARE_RUNG(gemm_v109_tma_umma_tmem_warpspecialized_persistent_2cta_streamk)  // v105 + stream-K
+KEBAB_DECLARE_RUNG(gemm_v110_tma_umma_tmem_warpspecialized_persistent_128x128)  // v104, 128 x 128 tiles
+KEBAB_DECLARE_RUNG(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64)   // v104, 128 x 64 tiles
 KEBAB_DECLARE_RUNG(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c)  // v105, row-major C
 #undef KEBAB_DECLARE_RUNG
 

@@ -40,6 +40,8 @@ const Rung kRungs[] = {
     {107, "tma_umma_tmem_warpspecialized_persistent_2cta_256x512", launch_v107_pair_wide},
     {108, "tma_umma_tmem_warpspecialized_persistent_streamk", launch_v108_streamk},
     {109, "tma_umma_tmem_warpspecialized_persistent_2cta_streamk", launch_v109_pair_streamk},
+    {110, "tma_umma_tmem_warpspecialized_persistent_128x128", launch_v110_persistent_n128},
+    {111, "tma_umma_tmem_warpspecialized_persistent_128x64", launch_v111_persistent_n64},
     {141, "tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c", launch_v105_pair},
 };
 
@@ -67,8 +69,8 @@ int map_reference_id(int v) {
 // The role of the reference's v20 heuristic (cuda_gemm.cu:25-77): choose a
 // decomposition from the tile count against the QUERIED SM count.
 // KEBAB_V120_MODE = dp | persistent | pair | wide | streamk (pairs) | streamk1
-// (1-CTA) | skinny | heuristic (default).
-int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc) {
+// (1-CTA) | n128 | n64 | skinny | heuristic (default).
+int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
     std::string m(env);
@@ -79,11 +81,15 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
     if (m == "WIDE" || m == "PAIRWIDE") return 107;
     if (m == "STREAMK" || m == "PAIRSTREAMK") return 109;
     if (m == "STREAMK1") return 108;
+    if (m == "N128" || m == "NARROW") return 110;
+    if (m == "N64") return 111;
     if ((m == "SKINNY" || m == "SPLITK") && rc_colc) return 106;
   }
-  // Decode-like shapes: too few 128-row tiles to occupy the GPU; stream B
-  // with the swap-AB split-K rung.
-  if (M <= 256 && rc_colc) return 106;
+  // Decode-like shapes: too few 128-row tiles to occupy the GPU, and enough
+  // of B (N x K >= 4 Mi elements) that streaming it dominates: the swap-AB
+  // split-K rung. Below that (256 x 1024 x 1024: 27 TFLOP/s on 106 against 67
+  // on 111) the small-problem tiles below win.
+  if (M <= 256 && rc_colc && N * K >= (int64_t)4 * 1024 * 1024) return 106;
   const int64_t pairs = sm_count / 2;
   const int64_t wide_tiles = ((M + 255) / 256) * ((N + 511) / 512);
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
@@ -96,15 +102,19 @@ int choose_v120(int64_t M, int64_t N, int64_t /*K*/, int sm_count, bool rc_colc)
   auto fill = [pairs](int64_t t) { return (double)t / (double)(((t + pairs - 1) / pairs) * pairs); };
   if (N % 512 == 0 && wide_tiles >= pairs && fill(wide_tiles) >= fill(pair_tiles) - 0.05) return 107;
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
-  // With 1..4 full waves and a partial last one, stream-K over the last two
-  // waves wins (measured at 4096^3 with 256 x 256 tiles: 103 vs 108 us); with less than one wave every tile
-  // would be split and the partial traffic costs more than it saves.
-  if (pair_tiles >= pairs) {
-    const int64_t waves = pair_tiles / pairs, rem = pair_tiles % pairs;
-    if (rem != 0 && waves <= 4) return 109;
-    return 105;
-  }
-  return 104;
+  // The stream-K rungs (108, 109) are not chosen here: measured against
+  // 105 they tie at 4096^3 and lose at 3072 x 2048 x 2048 (828 vs 953).
+  if (pair_tiles >= pairs) return 105;
+  // Small problems: the widest 128-row tiles that still occupy the SMs.
+  // 128 x 256 (v104) at 2048^3 and 4096 x 1024 x 1024; 128 x 128 (v110) at
+  // 1280^3 .. 1536^3 and 2048 x 1024 x 4096; 128 x 64 (v111, latency-bound
+  // sizes) up to 1024^3, where it beats cuBLAS below 1024^3.
+  const int64_t tm = (M + 127) / 128;
+  const int64_t t256 = tm * ((N + 255) / 256), t128 = tm * ((N + 127) / 128), t64 = tm * ((N + 63) / 64);
+  if (t256 * 10 >= (int64_t)sm_count * 8) return 104;
+  if (t128 <= sm_count && t128 * 10 >= (int64_t)sm_count * 6) return 110;
+  if (t64 <= sm_count) return 111;
+  return 110;
 }
 
 }  // namespace
@@ -222,6 +232,8 @@ KEBAB_RUNG_LAUNCHER(gemm_v106_tma_umma_tmem_swapab_splitk_cluster_skinny, 106)
 KEBAB_RUNG_LAUNCHER(gemm_v107_tma_umma_tmem_warpspecialized_persistent_2cta_256x512, 107)
 KEBAB_RUNG_LAUNCHER(gemm_v108_tma_umma_tmem_warpspecialized_persistent_streamk, 108)
 KEBAB_RUNG_LAUNCHER(gemm_v109_tma_umma_tmem_warpspecialized_persistent_2cta_streamk, 109)
+KEBAB_RUNG_LAUNCHER(gemm_v110_tma_umma_tmem_warpspecialized_persistent_128x128, 110)
+KEBAB_RUNG_LAUNCHER(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64, 111)
 KEBAB_RUNG_LAUNCHER(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c, 141)
 #undef KEBAB_RUNG_LAUNCHER
 

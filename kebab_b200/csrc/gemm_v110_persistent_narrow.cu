@@ -1,0 +1,14 @@
+// v110 / v111: the persistent 1-CTA kernel (v104) with narrower tiles for
+// problems whose 128 x 256 tiles would leave SMs idle: 128 x 128 tiles with a
+// 6-stage ring (v110) and 128 x 64 tiles with an 8-stage ring (v111), both
+// ~192 KB of operands in flight. At 1024^3, 128 x 256 tiles give 32 CTAs on
+// 148 SMs; 128 x 64 tiles give 128.
+// Kernel: gemm_umma.cuh; host launch template: gemm_umma_launch.cuh.
+#include "gemm_umma_launch.cuh"
+
+namespace kb {
+
+int launch_v110_persistent_n128(const GemmProblem& p) { return umma_launch::dispatch<1, true, 6, 128>(p); }
+int launch_v111_persistent_n64(const GemmProblem& p) { return umma_launch::dispatch<1, true, 8, 64>(p); }
+
+}  // namespace kb

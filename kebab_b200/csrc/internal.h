@@ -73,6 +73,8 @@ int launch_v106_skinny(const GemmProblem& p);
 int launch_v107_pair_wide(const GemmProblem& p);
 int launch_v108_streamk(const GemmProblem& p);
 int launch_v109_pair_streamk(const GemmProblem& p);
+int launch_v110_persistent_n128(const GemmProblem& p);
+int launch_v111_persistent_n64(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and

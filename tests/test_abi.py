@@ -84,18 +84,17 @@ def test_version_names_and_mapping():
 
 def test_v120_heuristic_without_gpu():
     # Falls back to 148 SMs when no device can be queried.
-    r_big = kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192)
-    r_small = kb.lib().kebab_resolve_version(120, kb.F16, 1024, 256, 8192)
-    r_skinny = kb.lib().kebab_resolve_version(120, kb.F16, 64, 8192, 8192)
-    r_mid = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 8192)
-    r_mid2 = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 4096)
-    # N % 512 != 0: 240 pair tiles = 3 full waves + a partial one -> stream-K.
-    r_sk = kb.lib().kebab_resolve_version(120, kb.F16, 4096, 3840, 4096)
-    # 160 wide tiles fill 72 % of the last wave against 86 % for 320 pair tiles.
-    r_sk2 = kb.lib().kebab_resolve_version(120, kb.F16, 2560, 8192, 4096)
-    c4a = kb.lib().kebab_resolve_version(120, kb.F16, 16384, 28672, 8192)
-    assert r_big == 107 and r_mid == 107 and r_mid2 == 107 and c4a == 107
-    assert r_sk == 109 and r_sk2 == 109 and r_small == 104 and r_skinny == 106
+    r = lambda M, N, K: kb.lib().kebab_resolve_version(120, kb.F16, M, N, K)
+    assert r(8192, 8192, 8192) == 107 and r(4096, 4096, 8192) == 107 and r(4096, 4096, 4096) == 107
+    assert r(16384, 28672, 8192) == 107
+    assert r(4096, 3840, 4096) == 105     # N % 512 != 0: 256 x 256 pair tiles
+    assert r(2560, 8192, 4096) == 105     # wide tiles fill the last wave worse
+    assert r(64, 8192, 8192) == 106 and r(128, 4096, 4096) == 106 and r(64, 2048, 2048) == 106
+    assert r(256, 1024, 1024) == 111      # too little of B for the skinny rung
+    assert r(2048, 2048, 2048) == 104 and r(4096, 1024, 1024) == 104
+    assert r(1536, 1536, 1536) == 110 and r(1280, 1280, 1280) == 110 and r(2048, 1024, 4096) == 110
+    assert r(1024, 1024, 1024) == 111 and r(512, 512, 512) == 111 and r(256, 256, 256) == 111
+    assert r(1024, 256, 8192) == 111
 
 
 def test_sparse24_tile_choice_without_gpu(monkeypatch):

@@ -11,7 +11,7 @@ from gemm_util import assert_close, inputs, run
 
 pytestmark = pytest.mark.gpu
 
-TC_RUNGS = [101, 102, 103, 104, 105, 107]
+TC_RUNGS = [101, 102, 103, 104, 105, 107, 110, 111]
 ALL_RUNGS = [1] + TC_RUNGS
 
 

@@ -44,7 +44,7 @@ def _run(cuda, M, N, K, opmode, version, dtype=O.F16, seed=0):
 
 
 @pytest.mark.parametrize("opmode", ["RC", "RR", "CR", "CC", "RCR", "RRR", "CRR", "CCR"])
-@pytest.mark.parametrize("version", [1, 103, 104, 105, 107, 108, 109, 120])
+@pytest.mark.parametrize("version", [1, 103, 104, 105, 107, 108, 109, 110, 111, 120])
 def test_layouts(cuda, opmode, version):
     _run(cuda, 384, 512, 320, opmode, version)
 
