@@ -112,6 +112,10 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
   const int64_t tm = (M + 127) / 128;
   const int64_t t256 = tm * ((N + 255) / 256), t128 = tm * ((N + 127) / 128), t64 = tm * ((N + 63) / 64);
   if (t256 * 10 >= (int64_t)sm_count * 8) return 104;
+  // Too few tiles and a deep K: split K over a cluster (rung 106 tiles M in
+  // 256-row blocks and reduces through distributed shared memory):
+  // 1024 x 1024 x 8192 672 vs 391 TFLOP/s, 2048 x 1024 x 4096 898 vs 666.
+  if (rc_colc && K >= 4096) return 106;
   if (t128 <= sm_count && t128 * 10 >= (int64_t)sm_count * 6) return 110;
   if (t64 <= sm_count) return 111;
   return 110;

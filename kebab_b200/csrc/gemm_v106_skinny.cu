@@ -1,4 +1,5 @@
-// v106: skinny / decode-shaped GEMM (M <= 256), HBM-bound.
+// v106: skinny / decode-shaped GEMM (M <= 256, HBM-bound), and, tiling M in
+// 256-row blocks, the split-K rung for problems with few tiles and a deep K.
 //
 // For M = 64, N = K = 8192 the work is 8.6 GFLOP but B is 128 MiB: the kernel
 // must stream B from HBM at full bandwidth, which needs far more CTAs than the
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(192, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = (int)cluster_ctarank();
   const int n0 = (blockIdx.x / SPLITS) * BMM;
+  const int m0 = blockIdx.y * BNM;  // M-tile (M > BNM)
   const int kb_total = (K + BK * KSUB - 1) / (BK * KSUB);
   const int kb_per = (kb_total + SPLITS - 1) / SPLITS;
   const int kb0 = min(kb_total, ks * kb_per);
@@ -153,7 +155,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int s = 0; s < KSUB; ++s) tma_load_2d(sBt + s * L::BT_SUB, &tmBt, &full[stage], k0 + s * BK, n0);
 #pragma unroll
-      for (int s = 0; s < KSUB; ++s) tma_load_2d(sA + s * L::A_SUB, &tmA, &full[stage], k0 + s * BK, 0);
+      for (int s = 0; s < KSUB; ++s) tma_load_2d(sA + s * L::A_SUB, &tmA, &full[stage], k0 + s * BK, m0);
       if (++stage == STAGES) {
         stage = 0;
         phase ^= 1u;
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(192, 1)
     // the peers' blocks are complete once recv_full flips.
     const bool got = SPLITS == 1 || mbar_wait(recv_full, 0, ctx, SITE_PARTIAL);
     if (threadIdx.x == 64) SKY_TRACE(12);
-    const int c0 = ks * CS;
+    const int c0 = m0 + ks * CS;
     const int n = n0 + row;
     T* out = C + (size_t)n * M;
     if (got && n < N) {
@@ -301,14 +303,15 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <typename T, int BNM, int KSUB, int STAGES, int SPLITS>
-int launch_splits(const GemmProblem& p, const CUtensorMap& tBt, const CUtensorMap& tA, int64_t tiles,
+int launch_splits(const GemmProblem& p, const CUtensorMap& tBt, const CUtensorMap& tA, int64_t tiles_n,
+                  int64_t tiles_m,
                   const WaitCtx& ctx) {
   using L = SkinnySmem<BNM, KSUB, STAGES>;
   auto kern = gemm_skinny_kernel<T, BNM, KSUB, STAGES, SPLITS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(tiles * SPLITS), 1, 1);
+  cfg.gridDim = dim3((unsigned)(tiles_n * SPLITS), (unsigned)tiles_m, 1);
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = L::ALLOC;
   cfg.stream = p.stream;
@@ -341,7 +344,8 @@ int launch(const GemmProblem& p, int splits_override) {
   CUtensorMap tBt, tA;
   if ((rc = make_tmap_2d(&tBt, p.B, p.dtype, p.N, p.K, p.K, BMM, BK, true))) return rc;
   if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.M, p.K, p.K, BNM, BK, true))) return rc;
-  const int64_t tiles = (p.N + BMM - 1) / BMM;
+  const int64_t tiles_n = (p.N + BMM - 1) / BMM, tiles_m = (p.M + BNM - 1) / BNM;
+  const int64_t tiles = tiles_n * tiles_m;
   const int kb_total = (int)((p.K + BK * KSUB - 1) / (BK * KSUB));
   int splits = splits_override;
   if (splits <= 0) {
@@ -351,12 +355,12 @@ int launch(const GemmProblem& p, int splits_override) {
     while (splits < 8 && tiles * splits * 2 <= (long long)L::PER_SM * dev->sm_count && splits * 2 <= kb_total)
       splits *= 2;
   }
-  if (tiles * splits > INT32_MAX) return fail(KEBAB_EINVAL, "grid too large for v106");
+  if (tiles_n * splits > INT32_MAX || tiles_m > 65535) return fail(KEBAB_EINVAL, "grid too large for v106");
   switch (splits) {
-    case 1: return launch_splits<T, BNM, KSUB, STAGES, 1>(p, tBt, tA, tiles, ctx);
-    case 2: return launch_splits<T, BNM, KSUB, STAGES, 2>(p, tBt, tA, tiles, ctx);
-    case 4: return launch_splits<T, BNM, KSUB, STAGES, 4>(p, tBt, tA, tiles, ctx);
-    case 8: return launch_splits<T, BNM, KSUB, STAGES, 8>(p, tBt, tA, tiles, ctx);
+    case 1: return launch_splits<T, BNM, KSUB, STAGES, 1>(p, tBt, tA, tiles_n, tiles_m, ctx);
+    case 2: return launch_splits<T, BNM, KSUB, STAGES, 2>(p, tBt, tA, tiles_n, tiles_m, ctx);
+    case 4: return launch_splits<T, BNM, KSUB, STAGES, 4>(p, tBt, tA, tiles_n, tiles_m, ctx);
+    case 8: return launch_splits<T, BNM, KSUB, STAGES, 8>(p, tBt, tA, tiles_n, tiles_m, ctx);
     default: return fail(KEBAB_EINVAL, "splits must be 1, 2, 4 or 8");
   }
 }
@@ -374,8 +378,7 @@ template <typename T>
 int launch_m(const GemmProblem& p, int splits) {
   if (p.M <= 64) return launch_cfg<T, 64>(p, splits);
   if (p.M <= 128) return launch_cfg<T, 128>(p, splits);
-  if (p.M <= 256) return launch_cfg<T, 256>(p, splits);
-  return fail(KEBAB_EINVAL, "v106 handles M <= 256 (use 104/105 for larger M)");
+  return launch_cfg<T, 256>(p, splits);  // M-tiles of 256
 }
 }  // namespace
 

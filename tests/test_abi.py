@@ -92,9 +92,11 @@ def test_v120_heuristic_without_gpu():
     assert r(64, 8192, 8192) == 106 and r(128, 4096, 4096) == 106 and r(64, 2048, 2048) == 106
     assert r(256, 1024, 1024) == 111      # too little of B for the skinny rung
     assert r(2048, 2048, 2048) == 104 and r(4096, 1024, 1024) == 104
-    assert r(1536, 1536, 1536) == 110 and r(1280, 1280, 1280) == 110 and r(2048, 1024, 4096) == 110
+    assert r(1536, 1536, 1536) == 110 and r(1280, 1280, 1280) == 110
+    assert r(2048, 1024, 4096) == 106 and r(1024, 1024, 8192) == 106 and r(512, 512, 8192) == 106  # split K
     assert r(1024, 1024, 1024) == 111 and r(512, 512, 512) == 111 and r(256, 256, 256) == 111
-    assert r(1024, 256, 8192) == 111
+    assert r(1024, 256, 8192) == 106
+    assert kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 8192) == 107
 
 
 def test_sparse24_tile_choice_without_gpu(monkeypatch):
