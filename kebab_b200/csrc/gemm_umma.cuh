@@ -284,6 +284,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   const WaitCtx& ctx = args.ctx;
 
   if (threadIdx.x == 0) {
+#ifdef KEBAB_SK_TRACE
+    g_sk_trace[((size_t)blockIdx.x * 8 + 7) * 8 + 5] = globaltimer();
+#endif
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
@@ -312,6 +315,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     pdl_wait();
     pdl_launch_dependents();
   }
+#ifdef KEBAB_SK_TRACE
+  if (threadIdx.x == 0) g_sk_trace[((size_t)blockIdx.x * 8 + 7) * 8 + 6] = globaltimer();
+#endif
 
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int cluster_id = blockIdx.x / CG;

@@ -12,3 +12,10 @@ int launch_v110_persistent_n128(const GemmProblem& p) { return umma_launch::disp
 int launch_v111_persistent_n64(const GemmProblem& p) { return umma_launch::dispatch<1, true, 8, 64>(p); }
 
 }  // namespace kb
+
+#ifdef KEBAB_SK_TRACE
+// Debug builds only: copy this translation unit's unit trace to the host.
+extern "C" int kebab_debug_sk_trace_v110(void* host, size_t bytes) {
+  return (int)cudaMemcpyFromSymbol(host, kb::g_sk_trace, bytes);
+}
+#endif
