@@ -107,3 +107,11 @@ def test_sparse24_tile_choice_without_gpu(monkeypatch):
     assert kb.sparse24_tile(8192, 8192) == (512, 160)
     monkeypatch.setenv("KEBAB_SPARSE_CG", "2")
     assert kb.sparse24_tile(8192, 8192) == (256, 256)
+
+
+@pytest.mark.parametrize("mode,rung", [("dp", 103), ("persistent", 104), ("pair", 105), ("wide", 107),
+                                       ("streamk", 109), ("streamk1", 108), ("n128", 110), ("n64", 111),
+                                       ("skinny", 106), ("heuristic", 107)])
+def test_v120_mode_override(monkeypatch, mode, rung):
+    monkeypatch.setenv("KEBAB_V120_MODE", mode)
+    assert kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192) == rung
