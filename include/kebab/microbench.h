@@ -24,6 +24,12 @@ int kebab_mbench_umma_once(int ab_bf16, int cta_group, float* host_out, int64_t 
  * whole GPU and SM cycles per instruction. */
 int kebab_mbench_umma(int cta_group, int n, int ab_bf16, int iters, double* tflops, double* cycles_per_mma);
 
+/* As kebab_mbench_umma for tcgen05.mma.sp (2:4 sparse A, FP16, K = 32
+ * logical per instruction): dense-equivalent TFLOP/s (2 * M * N * K_logical)
+ * and SM cycles per instruction. No reference counterpart (the reference's
+ * 2:4 probe is one mma.sp tile, kebab/lib/microbench/sparse_mma.cu). */
+int kebab_mbench_umma_sp(int cta_group, int n, int iters, double* tflops, double* cycles_per_mma);
+
 /* Issue-to-completion latency of one 128 x 256 x 16 MMA + commit + mbarrier
  * wait, averaged over `iters`, in SM cycles. */
 int kebab_mbench_umma_latency(int iters, double* cycles);

@@ -54,7 +54,9 @@ __device__ MbSmem mb_layout(uint8_t* raw) {
   return m;
 }
 
-template <int CG>
+// SP: tcgen05.mma.sp (2:4 A, K = 32 logical per instruction) with metadata
+// "keep elements 0 and 1" of every group copied into TMEM columns 256..259.
+template <int CG, bool SP = false>
 __global__ void __launch_bounds__(128, 1) umma_probe_kernel(int iters, int n, int bf16, float* out, long long* cycles,
                                                             WaitCtx ctx) {
   extern __shared__ uint8_t smem_raw[];
@@ -68,23 +70,39 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(int iters, int n, in
     mbar_init(m.bar, 1);
     fence_barrier_init();
   }
+  constexpr uint32_t COLS = SP ? 512 : 256;
+  if constexpr (SP) {
+    // Metadata block (128 rows x 16 bytes): nibble p0 | p1 << 2 = 0 | 1 << 2.
+    uint8_t* e = m.B + B_BYTES - 2048;
+    for (int i = threadIdx.x; i < 2048; i += blockDim.x) e[i] = 0x44;
+    fence_proxy_async_smem();
+  }
   if (warp == 0) {
-    tmem_alloc<CG>(m.slot, 256);
+    tmem_alloc<CG>(m.slot, COLS);
     tmem_relinquish<CG>();
   }
   tc_fence_before();
   if constexpr (CG == 2) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *m.slot;
-  const uint32_t idesc = umma_idesc_f16(128 * CG, n, bf16) ;
+  const uint32_t idesc = SP ? umma_idesc_f16_sparse(128 * CG, n, bf16) : umma_idesc_f16(128 * CG, n, bf16);
   if (threadIdx.x == 0 && rank == 0) {
+    if constexpr (SP)
+      tmem_cp_128x128b<CG>(tmem + 256, umma_desc(smem_u32(m.B + B_BYTES - 2048), 16, 128, 0));
     const long long t0 = clock64();
     for (int i = 0; i < iters; ++i) {
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const uint64_t ad = umma_desc_sw128(smem_u32(m.A) + k * 32), bd = umma_desc_sw128(smem_u32(m.B) + k * 32);
-        if constexpr (CG == 1) umma_f16_cg1(tmem, ad, bd, idesc, (i | k) != 0);
-        else umma_f16_cg2(tmem, ad, bd, idesc, (i | k) != 0);
+        if constexpr (SP) {
+          // A: 16 packed elements (32 bytes) per instruction; B: 32 K (64 bytes).
+          const uint64_t ad = umma_desc_sw128(smem_u32(m.A) + k * 32);
+          const uint64_t bd = umma_desc_sw128(smem_u32(m.B) + (k & 1) * 64);
+          umma_f16_sp<CG>(tmem, ad, bd, tmem + 256 + (uint32_t)(k & 2), idesc | (uint32_t)(k & 1), (i | k) != 0);
+        } else {
+          const uint64_t ad = umma_desc_sw128(smem_u32(m.A) + k * 32), bd = umma_desc_sw128(smem_u32(m.B) + k * 32);
+          if constexpr (CG == 1) umma_f16_cg1(tmem, ad, bd, idesc, (i | k) != 0);
+          else umma_f16_cg2(tmem, ad, bd, idesc, (i | k) != 0);
+        }
       }
     }
     if constexpr (CG == 1) umma_commit_cg1(m.bar);
@@ -110,7 +128,7 @@ __global__ void __launch_bounds__(128, 1) umma_probe_kernel(int iters, int n, in
   if constexpr (CG == 2) cluster_sync(); else __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc<CG>(tmem, 256);
+    tmem_dealloc<CG>(tmem, COLS);
   }
 }
 
@@ -239,12 +257,12 @@ int finish(cudaStream_t s, const char* what) {
   return kebab_device_status(reinterpret_cast<kebab_stream_t>(s), nullptr, 1);
 }
 
-template <int CG>
+template <int CG, bool SP = false>
 int launch_umma_probe(int grid_ctas, int iters, int n, int bf16, float* out, long long* cycles, cudaStream_t s) {
   WaitCtx ctx;
   int rc = wait_ctx(&ctx);
   if (rc) return rc;
-  auto kern = umma_probe_kernel<CG>;
+  auto kern = umma_probe_kernel<CG, SP>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, MB_SMEM);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   cudaLaunchConfig_t cfg = {};
@@ -316,6 +334,41 @@ int kebab_mbench_umma(int cta_group, int n, int ab_bf16, int iters, double* tflo
     long long mx = *std::max_element(h.begin(), h.end());
     // 4 MMAs of (128*cg) x n x 16 per iteration, per CTA (pair)
     const double flops = 2.0 * (128.0 * cta_group) * n * 64.0 * iters * (grid / cta_group);
+    if (tflops) *tflops = flops / (ev.ms() * 1e-3) / 1e12;
+    if (cycles_per_mma) *cycles_per_mma = (double)mx / (4.0 * iters);
+  }
+  cudaFree(cyc);
+  return rc;
+}
+
+
+int kebab_mbench_umma_sp(int cta_group, int n, int iters, double* tflops, double* cycles_per_mma) {
+  if ((cta_group != 1 && cta_group != 2) || n < 16 || n > 256 || n % 16 || iters <= 0)
+    return fail(KEBAB_EINVAL, "umma_sp: cta_group 1|2, n in 16..256 step 16, iters > 0");
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  const int grid = (dev->sm_count / cta_group) * cta_group;
+  long long* cyc = nullptr;
+  cudaError_t e = cudaMalloc(&cyc, sizeof(long long) * grid);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  Events ev;
+  rc = cta_group == 1 ? launch_umma_probe<1, true>(grid, std::max(1, iters / 10), n, 0, nullptr, cyc, nullptr)
+                      : launch_umma_probe<2, true>(grid, std::max(1, iters / 10), n, 0, nullptr, cyc, nullptr);
+  if (rc == KEBAB_OK) rc = finish(nullptr, "umma_sp warm-up");
+  if (rc == KEBAB_OK) {
+    cudaEventRecord(ev.a);
+    rc = cta_group == 1 ? launch_umma_probe<1, true>(grid, iters, n, 0, nullptr, cyc, nullptr)
+                        : launch_umma_probe<2, true>(grid, iters, n, 0, nullptr, cyc, nullptr);
+    cudaEventRecord(ev.b);
+    if (rc == KEBAB_OK) rc = finish(nullptr, "umma_sp bench");
+  }
+  if (rc == KEBAB_OK) {
+    std::vector<long long> h(grid / cta_group);
+    cudaMemcpy(h.data(), cyc, sizeof(long long) * h.size(), cudaMemcpyDeviceToHost);
+    long long mx = *std::max_element(h.begin(), h.end());
+    // 4 sparse MMAs of (128*cg) x n x 32 (logical K) per iteration, dense-equivalent FLOPs
+    const double flops = 2.0 * (128.0 * cta_group) * n * 128.0 * iters * (grid / cta_group);
     if (tflops) *tflops = flops / (ev.ms() * 1e-3) / 1e12;
     if (cycles_per_mma) *cycles_per_mma = (double)mx / (4.0 * iters);
   }

@@ -18,6 +18,7 @@ def _L():
     L.kebab_mbench_umma.argtypes = [c.c_int, c.c_int, c.c_int, c.c_int, c.POINTER(c.c_double),
                                     c.POINTER(c.c_double)]
     L.kebab_mbench_umma_latency.argtypes = [c.c_int, c.POINTER(c.c_double)]
+    L.kebab_mbench_umma_sp.argtypes = [c.c_int, c.c_int, c.c_int, c.POINTER(c.c_double), c.POINTER(c.c_double)]
     L.kebab_mbench_tmem_ld.argtypes = [c.c_int, c.POINTER(c.c_double), c.POINTER(c.c_double)]
     L.kebab_mbench_tma_load.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_int, c.POINTER(c.c_double)]
     return L
@@ -35,6 +36,13 @@ def umma(cta_group=1, n=256, bf16=False, iters=20000):
     t, c = ctypes.c_double(), ctypes.c_double()
     kb.check(_L().kebab_mbench_umma(cta_group, n, 1 if bf16 else 0, iters, ctypes.byref(t), ctypes.byref(c)))
     return t.value, c.value
+
+
+def umma_sp(cta_group=1, n=256, iters=20000):
+    """2:4 sparse MMA throughput: (dense-equivalent TFLOP/s, cycles per instruction)."""
+    t, cyc = ctypes.c_double(), ctypes.c_double()
+    kb.check(_L().kebab_mbench_umma_sp(cta_group, n, iters, ctypes.byref(t), ctypes.byref(cyc)))
+    return t.value, cyc.value
 
 
 def umma_latency(iters=1000):
@@ -67,6 +75,11 @@ def run_all():
             t, c = umma(cg, n)
             out["umma_cg%d_n%d" % (cg, n)] = {"tflops": t, "cycles_per_mma": c,
                                               "flops_per_clk_per_sm": 2 * 128 * n * 16 / c}
+    for cg in (1, 2):
+        for n in (128, 224, 256):
+            t, c = umma_sp(cg, n)
+            out["umma_sp_cg%d_n%d" % (cg, n)] = {"tflops_dense_equiv": t, "cycles_per_mma": c,
+                                                 "dense_equiv_flops_per_clk_per_sm": 2 * 128 * n * 32 / c}
     out["umma_latency_cycles"] = umma_latency()
     b, t = tmem_ld()
     out["tmem_ld"] = {"bytes_per_clk_per_sm": b, "tbps": t}

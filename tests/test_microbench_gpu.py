@@ -35,3 +35,15 @@ def test_latency_tmem_tma(cuda):
     for box in (64, 128, 256):
         gbs = mb.tma_load(buf, box)
         assert 500 < gbs < 12000, (box, gbs)
+
+
+@pytest.mark.parametrize("cg", [1, 2])
+def test_umma_sparse_throughput(cuda, cg):
+    """tcgen05.mma.sp issue rate: on CTA pairs at N = 256 the 2:4 MMA runs at
+    twice the dense rate (dense-equivalent FLOPs); single CTAs reach less."""
+    from kebab_b200 import microbench as mb
+    sp_tflops, sp_cyc = mb.umma_sp(cg, 256, iters=4000)
+    d_tflops, d_cyc = mb.umma(cg, 256, iters=4000)
+    assert 300 < sp_tflops < 5200, sp_tflops
+    ratio = sp_tflops / d_tflops
+    assert (ratio > 1.8) if cg == 2 else (ratio > 1.2), ratio
