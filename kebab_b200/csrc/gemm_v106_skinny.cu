@@ -23,6 +23,7 @@
 // require M % 64 or 128 == 0 and launch one CTA per 64..256-row tile).
 #include <algorithm>
 #include <cstdlib>
+#include <mutex>
 
 #include "gemm_umma.cuh"
 #include "internal.h"
@@ -308,7 +309,15 @@ int launch_splits(const GemmProblem& p, const CUtensorMap& tBt, const CUtensorMa
                   const WaitCtx& ctx) {
   using L = SkinnySmem<BNM, KSUB, STAGES>;
   auto kern = gemm_skinny_kernel<T, BNM, KSUB, STAGES, SPLITS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  // Shared-memory opt-in once per device (host cost, not per launch).
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  int dev = 0;
+  (void)cudaGetDevice(&dev);
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  });
+  cudaError_t e = attr_err[dev & 63];
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(tiles_n * SPLITS), (unsigned)tiles_m, 1);

@@ -9,6 +9,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <unordered_map>
 #include <utility>
 #include <vector>
 
@@ -113,18 +114,54 @@ static int get_encoder() {
   return KEBAB_OK;
 }
 
-int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
-                 uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
-  return make_tmap_2d_sw(out, base, dtype, rows, cols, ld, box_rows, box_cols, swizzle128 ? 128 : 0);
-}
+
+namespace {
+// Tensor maps are cached per (device, base pointer, dtype, shape, pitch, box,
+// swizzle): encoding one costs about a microsecond of host time, and a GEMM
+// needs three. Bounded: the map is cleared when it reaches kTmapCap entries
+// (callers cycling through many buffers re-encode), and by kebab_shutdown().
+struct TmapKey {
+  int dev, dtype, swizzle;
+  const void* base;
+  uint64_t rows, cols, ld;
+  uint32_t box_rows, box_cols;
+  bool operator==(const TmapKey& o) const {
+    return dev == o.dev && dtype == o.dtype && swizzle == o.swizzle && base == o.base && rows == o.rows &&
+           cols == o.cols && ld == o.ld && box_rows == o.box_rows && box_cols == o.box_cols;
+  }
+};
+struct TmapKeyHash {
+  size_t operator()(const TmapKey& k) const {
+    uint64_t h = reinterpret_cast<uintptr_t>(k.base) * 0x9E3779B97F4A7C15ull;
+    for (uint64_t v : {(uint64_t)k.dev, (uint64_t)k.dtype, (uint64_t)k.swizzle, k.rows, k.cols, k.ld,
+                       (uint64_t)k.box_rows << 32 | k.box_cols})
+      h = (h ^ v) * 0x100000001B3ull;
+    return (size_t)h;
+  }
+};
+constexpr size_t kTmapCap = 4096;
+std::mutex g_tmap_mu;
+std::unordered_map<TmapKey, CUtensorMap, TmapKeyHash> g_tmaps;
+}  // namespace
 
 int make_tmap_2d_sw(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
                     uint32_t box_rows, uint32_t box_cols, int swizzle_bytes) {
-  int rc = get_encoder();
-  if (rc) return rc;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
     return fail(KEBAB_EINVAL, "TMA operand base address is not 16-byte aligned");
   if ((ld * 2) % 16 != 0) return fail(KEBAB_EINVAL, "TMA operand row pitch is not a multiple of 16 bytes");
+  int dev = 0;
+  (void)cudaGetDevice(&dev);
+  const TmapKey key{dev, dtype, swizzle_bytes, base, rows, cols, ld, box_rows, box_cols};
+  {
+    std::lock_guard<std::mutex> lk(g_tmap_mu);
+    auto it = g_tmaps.find(key);
+    if (it != g_tmaps.end()) {
+      *out = it->second;
+      return KEBAB_OK;
+    }
+  }
+  int rc = get_encoder();
+  if (rc) return rc;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * 2};
   cuuint32_t box[2] = {box_cols, box_rows};
@@ -137,7 +174,15 @@ int make_tmap_2d_sw(CUtensorMap* out, const void* base, int dtype, uint64_t rows
                                               : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(KEBAB_EINVAL, "cuTensorMapEncodeTiled failed with CUresult " + std::to_string(r));
+  std::lock_guard<std::mutex> lk(g_tmap_mu);
+  if (g_tmaps.size() >= kTmapCap) g_tmaps.clear();
+  g_tmaps.emplace(key, *out);
   return KEBAB_OK;
+}
+
+int make_tmap_2d(CUtensorMap* out, const void* base, int dtype, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  return make_tmap_2d_sw(out, base, dtype, rows, cols, ld, box_rows, box_cols, swizzle128 ? 128 : 0);
 }
 
 int check_tma_shapes(const GemmProblem& p) {
@@ -264,6 +309,10 @@ int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us) {
 }
 
 void kebab_shutdown(void) {
+  {
+    std::lock_guard<std::mutex> lk(g_tmap_mu);
+    g_tmaps.clear();
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   for (auto& kv : g_sk)
     if (kv.second.base) cudaFree(kv.second.base);

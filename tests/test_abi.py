@@ -115,3 +115,10 @@ def test_sparse24_tile_choice_without_gpu(monkeypatch):
 def test_v120_mode_override(monkeypatch, mode, rung):
     monkeypatch.setenv("KEBAB_V120_MODE", mode)
     assert kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192) == rung
+
+
+def test_shutdown_is_idempotent_without_gpu():
+    # Frees workspaces and clears the tensor-map cache; safe to call repeatedly.
+    kb.lib().kebab_shutdown()
+    kb.lib().kebab_shutdown()
+    assert kb.lib().kebab_resolve_version(120, kb.F16, 8192, 8192, 8192) == 107
