@@ -209,6 +209,11 @@ struct UmmaArgs {
   uint32_t epi_backoff_ns;  // sleep between polls of the epilogue's accumulator wait (0 = spin)
   int l2_hint;              // 0: no hint; bits 0..1 policy of A, bits 2..3 of B (1 last, 2 first, 3 normal)
   int pdl = 0;              // launched with programmatic stream serialisation
+  // Whole tiles: odd units of a CTA walk K from the end, so each wave starts
+  // on the K-blocks the previous wave read last (still in L2). Off by default:
+  // it ties a tile's summation order to its place in the schedule, so results
+  // would no longer match bit for bit between a single GPU and M-shards.
+  int serp = 0;
   WaitCtx ctx;
 };
 
@@ -337,12 +342,15 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       UnitIter it;
       it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
       WorkUnit u;
+      int pu = 0;
       while (ok && it.next(u)) {
         int mb, nb;
         tile_coords(u.tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
         const int m0 = mb * BM_T + (int)rank * 128;
         const int n0 = nb * BN + (int)rank * (BN / CG);
-        for (int kb = u.k0; kb < u.k1; ++kb) {
+        const bool rev = !SK && args.serp && (pu++ & 1);
+        for (int i = 0; i < u.k1 - u.k0; ++i) {
+          const int kb = rev ? u.k1 - 1 - i : u.k0 + i;
           if (!mbar_wait(&empty[stage], phase ^ 1u, ctx, SITE_EMPTY)) {
             ok = false;
             break;
@@ -406,7 +414,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = u.k0; kb < u.k1; ++kb) {
+        for (int i = 0; i < u.k1 - u.k0; ++i) {
           if (!mbar_wait(&full[stage], phase, ctx, SITE_FULL)) {
             ok = false;
             break;
@@ -422,9 +430,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
               // Sub-MMA `sub` reads rows [128 sub, 128 sub + 128) of each CTA's B tile.
               const uint64_t bd = operand_desc<B_MN>(b_addr + sub * (128 * L::BK * 2), k);
               if constexpr (CG == 1)
-                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (kb != u.k0 || k != 0) ? 1u : 0u);
+                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
               else
-                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (kb != u.k0 || k != 0) ? 1u : 0u);
+                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
             }
           }
           any_issued = true;

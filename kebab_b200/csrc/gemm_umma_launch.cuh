@@ -176,6 +176,11 @@ int launch_umma(const GemmProblem& p) {
   cfg.attrs = attr;
   args.pdl = pdl_enabled() ? 1 : 0;
   cfg.numAttrs = args.pdl ? 2 : 1;
+  static const int serp_env = [] {
+    const char* e = std::getenv("KEBAB_SERPENTINE");
+    return (e && *e) ? std::atoi(e) : 0;
+  }();
+  args.serp = serp_env;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_umma_ws launch");
   return KEBAB_OK;

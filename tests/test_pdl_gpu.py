@@ -100,3 +100,35 @@ def test_pdl_off_gives_identical_bits(cuda):
 
     on, off = run(None), run("0")
     assert len(on) == len(CASES) and on == off
+
+
+_SERP_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import kebab_b200 as kb
+g = torch.Generator(device="cuda").manual_seed(11)
+M, N, K = 4096, 6144, 2048
+A = (torch.randn(M, K, device="cuda", generator=g) / K ** 0.5).half()
+B = (torch.randn(N, K, device="cuda", generator=g) / K ** 0.5).half()
+outs = []
+for v in (104, 105, 107):
+    c1 = kb.gemm(A, B, version=v); c2 = kb.gemm(A, B, version=v)
+    torch.cuda.synchronize()
+    ref = (A.float() @ B.float().t()).t()
+    rel = ((c1.float() - ref).norm() / ref.norm()).item()
+    outs.append("%d %d %.3e" % (v, int(torch.equal(c1, c2)), rel))
+print(";".join(outs))
+"""
+
+
+@pytest.mark.gpu
+def test_serpentine_k_order_opt_in(cuda):
+    """KEBAB_SERPENTINE=1 (reverse K on alternate tiles of a CTA) stays
+    deterministic and within the FP16 tolerance of an FP32 reference."""
+    env = dict(os.environ, KEBAB_SERPENTINE="1")
+    r = subprocess.run([sys.executable, "-c", _SERP_SCRIPT, ROOT], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    for item in r.stdout.strip().split(";"):
+        v, same, rel = item.split()
+        assert same == "1" and float(rel) < 1e-3, item
