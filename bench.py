@@ -179,7 +179,9 @@ def cpu_baseline_port(M, N, K, target_s):
     t0 = time.perf_counter()
     O.gemm_rows(A, B, rows, Mp, N, K, O.F16, threads)
     dt = time.perf_counter() - t0
-    n_rows = int(max(len(rows), min(Mp, round(len(rows) * target_s / max(dt, 1e-3)))))
+    # Enough rows for about target_s of CPU work; rows cycle over the Mp
+    # generated ones (each row reads all of B, so repeats cost the same).
+    n_rows = int(max(len(rows), min(64 * Mp, round(len(rows) * target_s / max(dt, 1e-3)))))
     rows = np.arange(n_rows, dtype=np.int64) % Mp
     t0 = time.perf_counter()
     O.gemm_rows(A, B, rows, Mp, N, K, O.F16, threads)
