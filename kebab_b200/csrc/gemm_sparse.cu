@@ -401,35 +401,33 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   args.epi_backoff_ns = 0;
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   auto kern = gemm_sparse_kernel<T, CG, STAGES, MT, BN>;
+  // Once per device and instantiation: the shared-memory opt-in and, for
+  // pairs, how many clusters fit.
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
+  static int max_active[64];
   const int di = dev->device & 63;
   std::call_once(once[di], [&] {
     attr_err[di] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    max_active[di] = dev->sm_count / CG;
+    if (attr_err[di] != cudaSuccess || CG == 1) return;
+    cudaLaunchConfig_t qc = {};
+    qc.gridDim = dim3(CG * (dev->sm_count / CG), 1, 1);
+    qc.blockDim = dim3(Cfg::THREADS, 1, 1);
+    qc.dynamicSmemBytes = L::ALLOC;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = CG;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &qc) == cudaSuccess && n > 0) max_active[di] = n;
+    (void)cudaGetLastError();
   });
   if (attr_err[di] != cudaSuccess) return cuda_fail(attr_err[di], "cudaFuncSetAttribute");
-  int max_clusters = dev->sm_count / CG;
-  if (CG > 1) {
-    static int max_active[64] = {0};
-    if (max_active[di] == 0) {
-      cudaLaunchConfig_t qc = {};
-      qc.gridDim = dim3(CG * max_clusters, 1, 1);
-      qc.blockDim = dim3(Cfg::THREADS, 1, 1);
-      qc.dynamicSmemBytes = L::ALLOC;
-      cudaLaunchAttribute qa[1];
-      qa[0].id = cudaLaunchAttributeClusterDimension;
-      qa[0].val.clusterDim.x = CG;
-      qa[0].val.clusterDim.y = 1;
-      qa[0].val.clusterDim.z = 1;
-      qc.attrs = qa;
-      qc.numAttrs = 1;
-      int n = 0;
-      cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
-      max_active[di] = (e == cudaSuccess && n > 0) ? n : max_clusters;
-      (void)cudaGetLastError();
-    }
-    max_clusters = std::min(max_clusters, max_active[di]);
-  }
+  const int max_clusters = std::min(dev->sm_count / CG, max_active[di]);
   const int clusters = (int)std::min<long long>(tiles, max_clusters);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(CG * clusters, 1, 1);

@@ -80,39 +80,36 @@ int launch_umma(const GemmProblem& p) {
   if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
 
   auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>;
+  // Once per device and instantiation: the shared-memory opt-in and, for
+  // pairs (which must be co-resident on a GPC), how many clusters fit.
   static std::once_flag attr_once[64];
   static cudaError_t attr_err[64];
+  static int max_active[64];
   const int di = dev->device & 63;
   std::call_once(attr_once[di], [&] {
     attr_err[di] = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    max_active[di] = dev->sm_count / CG;
+    if (attr_err[di] != cudaSuccess || CG == 1) return;
+    cudaLaunchConfig_t qc = {};
+    qc.gridDim = dim3(CG * (dev->sm_count / CG), 1, 1);
+    qc.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
+    qc.dynamicSmemBytes = L::ALLOC;
+    cudaLaunchAttribute qa[1];
+    qa[0].id = cudaLaunchAttributeClusterDimension;
+    qa[0].val.clusterDim.x = CG;
+    qa[0].val.clusterDim.y = 1;
+    qa[0].val.clusterDim.z = 1;
+    qc.attrs = qa;
+    qc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &qc) == cudaSuccess && n > 0) max_active[di] = n;
+    (void)cudaGetLastError();
   });
   if (attr_err[di] != cudaSuccess) return cuda_fail(attr_err[di], "cudaFuncSetAttribute(max dynamic smem)");
 
   int clusters;
   if (PERSISTENT) {
-    int max_clusters = dev->sm_count / CG;
-    if (CG > 1) {
-      // Pairs must be co-resident on a GPC; ask the occupancy API how many fit.
-      static int max_active[64] = {0};
-      if (max_active[di] == 0) {
-        cudaLaunchConfig_t qc = {};
-        qc.gridDim = dim3(CG * max_clusters, 1, 1);
-        qc.blockDim = dim3(UmmaEpi<BN>::THREADS, 1, 1);
-        qc.dynamicSmemBytes = L::ALLOC;
-        cudaLaunchAttribute qa[1];
-        qa[0].id = cudaLaunchAttributeClusterDimension;
-        qa[0].val.clusterDim.x = CG;
-        qa[0].val.clusterDim.y = 1;
-        qa[0].val.clusterDim.z = 1;
-        qc.attrs = qa;
-        qc.numAttrs = 1;
-        int n = 0;
-        cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
-        max_active[di] = (e == cudaSuccess && n > 0) ? n : max_clusters;
-        (void)cudaGetLastError();
-      }
-      max_clusters = std::min(max_clusters, max_active[di]);
-    }
+    int max_clusters = std::min(dev->sm_count / CG, max_active[di]);
     // Stream-K spreads K-iterations over every SM, even with fewer tiles.
     clusters = SK ? max_clusters : (int)std::min<long long>(tiles, max_clusters);
   } else {
