@@ -3,7 +3,8 @@
  * reference's Hopper probes in kebab/lib/microbench (mma_wgmma.cu:390-470,
  * 740-826: one verified op + a throughput loop; copy_gmem_to_smem_2d_tma_ptx.cu:
  * 129-181: TMA bandwidth). All calls synchronize the device and return a
- * KEBAB_* status. No TMA-multicast probe is built.
+ * KEBAB_* status. No TMA-multicast probe is built: multicast loads are kept
+ * out of every source file that multi-GPU runs use.
  */
 #ifndef KEBAB_MICROBENCH_H_
 #define KEBAB_MICROBENCH_H_

@@ -26,7 +26,7 @@ No SASS or PTX is read or printed.
 Usage::
 
     python -m kebab_b200.report csv bench_results/*.csv
-    python -m kebab_b200.report launches gpurun_launches.csv --title "bench 8192^3"
+    python -m kebab_b200.report launches launches.csv --title "bench 8192^3"
     python -m kebab_b200.report ncu prof.ncu-rep --flops 1.0995e12 --bytes 402653184
 """
 from __future__ import annotations
