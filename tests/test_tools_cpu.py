@@ -158,3 +158,22 @@ def test_report_cli_launches(tmp_path):
     o = tmp_path / "o.md"
     assert report.main(["launches", str(p), "-o", str(o)]) == 0
     assert "gemm_kernel" in o.read_text()
+
+
+def test_profile_commands_are_safe():
+    from kebab_b200 import profile
+    plain, cap = profile.commands(107, 4096, 4096, 4096, "float16", "RC", Path("x/y"), "full", 1, "gemm_umma")
+    assert plain[0].endswith("runonce_gemm") and "--version" in plain
+    assert cap[:2] == ["ncu", "--set"] and "--clock-control" in cap and cap[cap.index("--clock-control") + 1] == "none"
+    assert cap[cap.index("-c") + 1] == "1" and cap[cap.index("-k") + 1] == "regex:gemm_umma"
+    assert cap[-len(plain):] == plain  # ncu profiles exactly the command that ran plainly
+    with pytest.raises(ValueError):
+        profile.commands(107, 64, 64, 64, "float16", "RC", Path("x"), "full", 5, "gemm")
+
+
+def test_profile_refuses_large_problems(capsys):
+    from kebab_b200 import profile
+    assert profile.main(["--m", "32768", "--n", "32768", "--k", "32768", "--dry-run"]) == 2
+    assert profile.main(["--m", "1024", "--n", "1024", "--k", "1024", "--dry-run"]) == 0
+    out = capsys.readouterr().out
+    assert "--clock-control none" in out
