@@ -200,14 +200,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-// Prefetch one tensor-map box into L2 (no shared memory, no barrier).
-__device__ __forceinline__ void tma_prefetch_l2_2d(const void* tmap, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
-                   reinterpret_cast<uint64_t>(tmap)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 // L2 eviction-priority policies for the cache-hinted loads below.
 __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
