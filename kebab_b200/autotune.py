@@ -40,7 +40,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 
 REPO = Path(__file__).resolve().parents[1]
 DEFAULT_BENCH = REPO / "kebab_b200" / "bin" / "bench_gemm"
-V120_MODES = ("heuristic", "dp", "persistent", "pair", "wide", "streamk", "streamk1", "skinny")
+V120_MODES = ("heuristic", "dp", "persistent", "pair", "wide", "streamk", "streamk1", "skinny", "n128", "n64")
 
 Problem = Tuple[int, int, int]
 

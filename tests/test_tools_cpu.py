@@ -177,3 +177,15 @@ def test_profile_refuses_large_problems(capsys):
     assert profile.main(["--m", "1024", "--n", "1024", "--k", "1024", "--dry-run"]) == 0
     out = capsys.readouterr().out
     assert "--clock-control none" in out
+
+
+def test_autotune_modes_match_the_v120_parser():
+    """Every KEBAB_V120_MODE value the C++ dispatcher accepts (its primary
+    spelling) is a mode autotune can sweep, and no other."""
+    import re
+
+    src = (Path(__file__).resolve().parents[1] / "kebab_b200" / "csrc" / "gemm_api.cu").read_text()
+    body = src[src.index("int choose_v120("):]
+    body = body[:body.index("// Decode-like shapes")]
+    parsed = {m.group(1).lower() for m in re.finditer(r'if \(\(?m == "(\w+)"', body)}
+    assert parsed | {"heuristic"} == set(autotune.V120_MODES)
