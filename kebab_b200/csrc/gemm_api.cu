@@ -114,8 +114,10 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
   if (t256 * 10 >= (int64_t)sm_count * 8) return 104;
   // Too few tiles and a deep K: split K over a cluster (rung 106 tiles M in
   // 256-row blocks and reduces through distributed shared memory):
-  // 1024 x 1024 x 8192 672 vs 391 TFLOP/s, 2048 x 1024 x 4096 898 vs 666.
-  if (rc_colc && K >= 4096) return 106;
+  // 1024 x 1024 x 8192 672 vs 391 TFLOP/s, 2048 x 1024 x 4096 898 vs 666,
+  // 1536 x 1536 x 3072 819 vs 682. At K = 1536 (1536^3: 533 vs 569) and
+  // 1280 the 128 x 128 tiles still win.
+  if (rc_colc && K >= 3072) return 106;
   if (t128 <= sm_count && t128 * 10 >= (int64_t)sm_count * 6) return 110;
   if (t64 <= sm_count) return 111;
   return 110;

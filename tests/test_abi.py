@@ -96,6 +96,7 @@ def test_v120_heuristic_without_gpu():
     assert r(2048, 1024, 4096) == 106 and r(1024, 1024, 8192) == 106 and r(512, 512, 8192) == 106  # split K
     assert r(1024, 1024, 1024) == 111 and r(512, 512, 512) == 111 and r(256, 256, 256) == 111
     assert r(1024, 256, 8192) == 106
+    assert r(1536, 1536, 3072) == 106 and r(1536, 1536, 2048) == 110
     assert kb.lib().kebab_resolve_version(120, kb.F16, 4096, 4096, 8192) == 107
 
 
