@@ -167,6 +167,45 @@ def make_inputs(torch, M, N, K, dtype, device, seed):
     return A, B
 
 
+def cpu_model():
+    """The host CPU's model name (first `model name` line of /proc/cpuinfo)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+def cpu_reference_1core(M, N, K, n=512):
+    """referenceGemmCpp<float> as the reference ships it (single thread,
+    compiled from its own header into oracle/_ref) at n^3 on the C1 inputs
+    (mt19937(0) uniform[-1, 1], FP16), with the time it would take for the
+    full M x N x K workload extrapolated from its rate. Falls back to the
+    restatement on one thread when oracle/_ref is not built."""
+    import oracle as O
+    A, B = O.fill_pair(n, n, n, seed=0, dtype=O.F16, dist=O.UNIFORM)
+    L = O.ref()
+    if L is not None:
+        Af = np.ascontiguousarray(O.to_float(A, O.F16), np.float32)
+        Bf = np.ascontiguousarray(O.to_float(B, O.F16), np.float32)
+        C = np.empty(n * n, np.float32)
+        t0 = time.perf_counter()
+        L.kbr_gemm_f32(Af, Bf, C, n, n, n)
+        dt = time.perf_counter() - t0
+        kind = "reference"
+    else:
+        t0 = time.perf_counter()
+        O.gemm(A, B, n, n, n, O.F16, threads=1)
+        dt = time.perf_counter() - t0
+        kind = "port"
+    gflops = 2.0 * n ** 3 / dt / 1e9
+    return {"gflops": gflops, "cores": 1, "kind": kind, "size": "%d^3" % n, "seconds": dt,
+            "extrapolated_s_full_workload": 2.0 * M * N * K / (gflops * 1e9)}
+
+
 def cpu_baseline_port(M, N, K, target_s):
     """The oracle restatement (bit-identical to referenceGemmCpp<float>) on all
     host cores over a bounded row sample of the workload."""
@@ -555,6 +594,10 @@ def main():
     if world == 1 and not args.no_cpu_baseline:
         try:
             out["cpu_baseline"] = cpu_baseline_port(M, N, K, args.cpu_seconds)
+            cb = out["cpu_baseline"]
+            cb["cpu_model"] = cpu_model()
+            cb["extrapolated_s_full_workload"] = 2.0 * M * N * K / (cb["value"] * 1e12)
+            cb["reference_1core"] = cpu_reference_1core(M, N, K)
         except Exception as e:
             out["cpu_baseline"] = {"unavailable": str(e)}
     print(json.dumps(out))

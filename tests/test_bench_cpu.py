@@ -38,3 +38,14 @@ def test_cpu_baseline_port():
     import bench
     d = bench.cpu_baseline_port(64, 256, 256, 0.2)
     assert d["kind"] == "port" and d["value"] > 0 and d["cores"] >= 1 and "rows" in d["sample"]
+
+
+def test_cpu_reference_1core():
+    sys.path.insert(0, ROOT)
+    import bench
+    d = bench.cpu_reference_1core(8192, 8192, 8192, n=64)
+    assert d["cores"] == 1 and d["gflops"] > 0 and d["kind"] in ("reference", "port")
+    assert abs(d["extrapolated_s_full_workload"] - 2.0 * 8192 ** 3 / (d["gflops"] * 1e9)) < 1e-6 * d[
+        "extrapolated_s_full_workload"]
+    m = bench.cpu_model()
+    assert m is None or isinstance(m, str)
