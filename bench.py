@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--workload", default="dense", choices=["dense", "sparse24"],
                    help="dense GEMM (BASELINE config 2) or 2:4 sparse GEMM (config 5)")
     p.add_argument("--e2e-steps", type=int, default=20)
+    p.add_argument("--bcast-chunks", type=int, default=4,
+                   help="N-chunks of the pipelined broadcast + GEMM measurement (N > 1 GPUs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work for the cpu_baseline sample")
@@ -345,6 +347,9 @@ def main():
         Cs.append(torch.empty((N, M), dtype=dtype, device=device))
     bcast_ms = None
     if world > 1:
+        # The first large broadcast sets up NCCL's channels and buffers (~18 ms
+        # on two B200s): do it once untimed (rank 0's B is unchanged by it).
+        dist.broadcast(Bs[0], src=0)
         dist.barrier()
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -437,6 +442,36 @@ def main():
     total_ms = float(t.item())
     flops_rank = 2.0 * M * N * K
     value = world * flops_rank * args.steps / (total_ms * 1e-3) / 1e12
+
+    # First-call latency with the broadcast in it (N > 1, dense): broadcast
+    # of B then the GEMM, against the pipelined form that broadcasts B in
+    # N-chunks and starts each chunk's GEMM as soon as it has arrived. Device
+    # time, max over ranks, median of 3.
+    bcast_gemm = None
+    if world > 1 and not sparse:
+        from kebab_b200.shard import broadcast_gemm_pipelined
+
+        def one(pipelined):
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            if pipelined:
+                broadcast_gemm_pipelined(As[0], Bs[0], Cs[0], chunks=args.bcast_chunks, version=version, stream=stream)
+            else:
+                dist.broadcast(Bs[0], src=0)
+                kb.gemm(As[0], Bs[0], Cs[0], version=version, stream=stream)
+            b.record(stream)
+            torch.cuda.synchronize()
+            tt = torch.tensor([a.elapsed_time(b)], device=device, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            return float(tt.item())
+
+        one(True)  # warm-up of the chunk shapes
+        ser = sorted(one(False) for _ in range(3))[1]
+        pip = sorted(one(True) for _ in range(3))[1]
+        bcast_gemm = {"serial_ms": ser, "pipelined_ms": pip, "chunks": args.bcast_chunks,
+                      "what": "broadcast of B + this rank's GEMM, device time, max over ranks, median of 3"}
 
     # End to end through the public API with host buffers: every step copies
     # its inputs host -> device from pinned memory (A shard; B on rank 0, then
@@ -585,6 +620,7 @@ def main():
         "gpu_launches": args.steps,
         "clocks": clocks,
         "broadcast_ms": bcast_ms,
+        "broadcast_gemm": bcast_gemm,
         "cublas": cublas,
     }
     if sparse:

@@ -61,6 +61,54 @@ def sharded_gemm(A_shard, B, C_shard=None, version=120, gemm_fn=None, stream=Non
     return gemm_fn(A_shard, B, C_shard)
 
 
+def chunk_bounds(N, chunks, align=256):
+    """Column ranges [n0, n1) of `chunks` N-chunks of B, each a multiple of
+    `align` columns (the widest tile) except the last; fewer chunks when N
+    is small."""
+    if N <= 0 or chunks <= 0:
+        raise ShardError("bad N=%d or chunks=%d" % (N, chunks))
+    step = -(-N // chunks)
+    step = -(-step // align) * align
+    return [(n0, min(N, n0 + step)) for n0 in range(0, N, step)]
+
+
+def broadcast_gemm_pipelined(A_shard, B, C_shard=None, chunks=4, src=0, version=120, gemm_fn=None, stream=None,
+                             group=None):
+    """Broadcast of B overlapped with this rank's GEMM: B ([N, K], column-
+    major K x N, so an N-chunk is a contiguous slab) is broadcast from `src`
+    in `chunks` pieces, all issued at once; the GEMM of chunk i (columns
+    [n0, n1) of the [N, rows] C shard, also contiguous) starts as soon as
+    chunk i has arrived, while later chunks are still in flight. On NCCL
+    ranks the wait on a chunk is a stream dependency, not a host block.
+    Each element of C is computed from the same A row and B column in the
+    same K order as by sharded_gemm with a fixed rung, so the results match
+    it bit for bit. Returns C_shard.
+
+    Measured on two B200s it is slower than broadcast-then-GEMM (32768^3
+    BF16, 4 chunks: 37.4 ms against 29.1; 8192^3 FP16: 1.12 against 1.05):
+    the persistent rungs size their grid to every SM, so NCCL's broadcast
+    kernels and the chunk GEMMs contend for SMs instead of overlapping, and
+    over NVLink the broadcast is a small share of the serial time (32768^3:
+    ~3.6 of 29.1 ms)."""
+    import torch
+    import torch.distributed as dist
+    N = B.shape[0]
+    rows = A_shard.shape[0]
+    if C_shard is None:
+        C_shard = torch.empty((N, rows), dtype=B.dtype, device=B.device)
+    bounds = chunk_bounds(N, chunks)
+    multi = dist.is_initialized() and dist.get_world_size(group) > 1
+    works = [dist.broadcast(B[n0:n1], src=src, group=group, async_op=True) if multi else None
+             for n0, n1 in bounds]
+    for (n0, n1), w in zip(bounds, works):
+        if w is not None:
+            w.wait()
+        out = sharded_gemm(A_shard, B[n0:n1], C_shard[n0:n1], version=version, gemm_fn=gemm_fn, stream=stream)
+        if out is not None and out.data_ptr() != C_shard[n0:n1].data_ptr():
+            C_shard[n0:n1].copy_(out)
+    return C_shard
+
+
 def gather_c(C_shard, world, group=None):
     """All-gathers the [N, rows] shards into the global column-major C
     ([N, rows*world]): column j of C is the concatenation of every rank's

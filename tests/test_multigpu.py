@@ -18,7 +18,7 @@ CHILD = r'''
 import os, sys, torch, torch.distributed as dist
 sys.path.insert(0, os.environ["KB_ROOT"])
 import kebab_b200 as kb
-from kebab_b200.shard import row_block, shard_a, broadcast_b, sharded_gemm, gather_c
+from kebab_b200.shard import row_block, shard_a, broadcast_b, broadcast_gemm_pipelined, sharded_gemm, gather_c
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
 torch.cuda.set_device(rank)
 dev = torch.device("cuda", rank)
@@ -29,9 +29,12 @@ A = (torch.randn(M, K, generator=g, device=dev) / K ** 0.5).half()
 B = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).half()
 if rank != 0:
     B.zero_()
-broadcast_b(B, src=0)
 blk = row_block(M, world, rank)
-C = sharded_gemm(shard_a(A, blk).contiguous(), B, version=int(os.environ["KB_VERSION"]))
+if os.environ.get("KB_PIPELINE"):
+    C = broadcast_gemm_pipelined(shard_a(A, blk).contiguous(), B, chunks=3, version=int(os.environ["KB_VERSION"]))
+else:
+    broadcast_b(B, src=0)
+    C = sharded_gemm(shard_a(A, blk).contiguous(), B, version=int(os.environ["KB_VERSION"]))
 torch.cuda.synchronize()
 assert kb.device_status()[0] == kb.OK
 Cg = gather_c(C, world)
@@ -53,8 +56,8 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("version", [104, 105])
-def test_sharded_bitexact(cuda, version):
+@pytest.mark.parametrize("version,pipeline", [(104, ""), (105, ""), (105, "1")])
+def test_sharded_bitexact(cuda, version, pipeline):
     import torch
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
@@ -63,7 +66,8 @@ def test_sharded_bitexact(cuda, version):
     procs = []
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
-                   MASTER_PORT=str(port), KB_ROOT=ROOT, KB_VERSION=str(version), NCCL_NVLS_ENABLE="0")
+                   MASTER_PORT=str(port), KB_ROOT=ROOT, KB_VERSION=str(version), KB_PIPELINE=pipeline,
+                   NCCL_NVLS_ENABLE="0")
         procs.append(subprocess.Popen([sys.executable, "-c", CHILD], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     outs = [p.communicate(timeout=300)[0] for p in procs]

@@ -12,7 +12,8 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from kebab_b200.shard import ShardError, gather_c, row_block, shard_a, broadcast_b, sharded_gemm
+from kebab_b200.shard import (ShardError, broadcast_b, broadcast_gemm_pipelined, chunk_bounds, gather_c, row_block,
+                              shard_a, sharded_gemm)
 
 
 def _free_port():
@@ -45,7 +46,16 @@ def _oracle_gemm(A, B, C):
     return torch.from_numpy(c.reshape(N, M)).to(torch.float16)
 
 
-def _worker(rank, world, port, M, N, K, q):
+def test_chunk_bounds():
+    assert chunk_bounds(8192, 4) == [(0, 2048), (2048, 4096), (4096, 6144), (6144, 8192)]
+    assert chunk_bounds(1000, 4) == [(0, 256), (256, 512), (512, 768), (768, 1000)]
+    assert chunk_bounds(48, 4) == [(0, 48)]      # one 256-aligned chunk covers it
+    assert chunk_bounds(1, 1) == [(0, 1)]
+    with pytest.raises(ShardError):
+        chunk_bounds(0, 4)
+
+
+def _worker(rank, world, port, M, N, K, q, pipelined=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -54,9 +64,13 @@ def _worker(rank, world, port, M, N, K, q):
         A_glob = (torch.randn(M, K, generator=g) / K ** 0.5).to(torch.float16)
         B = (torch.randn(N, K, generator=g) / K ** 0.5).to(torch.float16) if rank == 0 \
             else torch.zeros(N, K, dtype=torch.float16)
-        broadcast_b(B, src=0)
         blk = row_block(M, world, rank)
-        C_shard = sharded_gemm(shard_a(A_glob, blk).contiguous(), B, gemm_fn=lambda a, b, c: _oracle_gemm(a, b, c))
+        stand_in = lambda a, b, c: _oracle_gemm(a, b, c)
+        if pipelined:
+            C_shard = broadcast_gemm_pipelined(shard_a(A_glob, blk).contiguous(), B, chunks=3, gemm_fn=stand_in)
+        else:
+            broadcast_b(B, src=0)
+            C_shard = sharded_gemm(shard_a(A_glob, blk).contiguous(), B, gemm_fn=stand_in)
         C = gather_c(C_shard, world)
         if rank == 0:
             q.put(C.view(torch.int16).numpy().copy())
@@ -64,13 +78,14 @@ def _worker(rank, world, port, M, N, K, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_sharded_equals_unsharded(world):
-    M, N, K = 64 * world, 48, 40
+@pytest.mark.parametrize("world,pipelined,N", [(2, False, 48), (4, False, 48), (2, True, 600), (4, True, 520)])
+def test_sharded_equals_unsharded(world, pipelined, N):
+    # pipelined: B broadcast in 256-column chunks overlapped with the per-chunk GEMMs.
+    M, K = 64 * world, 40
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, N, K, q, pipelined)) for r in range(world)]
     for p in procs:
         p.start()
     got = q.get(timeout=120)
