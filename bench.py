@@ -633,7 +633,10 @@ def main():
             cb = out["cpu_baseline"]
             cb["cpu_model"] = cpu_model()
             cb["extrapolated_s_full_workload"] = 2.0 * M * N * K / (cb["value"] * 1e12)
-            cb["reference_1core"] = cpu_reference_1core(M, N, K)
+            try:
+                cb["reference_1core"] = cpu_reference_1core(M, N, K)
+            except Exception as e:
+                cb["reference_1core"] = {"unavailable": str(e)}
         except Exception as e:
             out["cpu_baseline"] = {"unavailable": str(e)}
     print(json.dumps(out))
