@@ -96,10 +96,15 @@ int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us);
  * memory budget, a plugin host that forbids allocation after start-up. Its
  * scratch is a static device array present on every GPU that loads the
  * library: 160 partial-tile slots of 128 KiB (20 MiB) plus 2.5 KiB of flags;
- * a device whose grid needs more than 160 CTAs gets KEBAB_ENOTSUP. The first
- * call on a device sets up (looks up the array's address); make it before any
- * stream capture. All calls share the array, so calls that overlap on the GPU
- * race. No counterpart in the reference. */
+ * a device whose grid needs more than 160 CTAs gets KEBAB_ENOTSUP. A
+ * per-device set-up looks up the array's address and opts the kernels in; it
+ * is also when the driver loads this code onto the device and commits the
+ * 20 MiB, so it is the one step that may allocate. It runs on the first call
+ * on a device, or alone when called with null A, B, C and M = N = K = 0 (then
+ * it returns KEBAB_OK and launches nothing): make it before the code that must
+ * not allocate and before any stream capture. Later calls allocate nothing.
+ * All calls share the array, so calls that overlap on the GPU race.
+ * kebab_shutdown() forgets the set-up. No counterpart in the reference. */
 int kebab_gemm_streamk_noalloc(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N,
                                int64_t K, kebab_stream_t stream);
 

@@ -73,7 +73,7 @@ def build(force=False, jobs=None, verbose=False):
         with open(os.path.join(BUILD, "ptxas.txt"), "w") as f:
             f.write(report)
     if force or _mtime(LIB) < max(_mtime(o) for o in objs):
-        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcuda" if False else "-lcudart_static", "-ldl",
+        cmd = [NVCC, *ARCH, "-shared", "-o", LIB, *objs, "-lcudart_static", "-ldl",
                "-lpthread", "-lrt"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:

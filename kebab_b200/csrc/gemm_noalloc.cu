@@ -13,13 +13,18 @@
 // each, one per CTA) = 20 MiB, plus kNoallocSlots * 4 flags. A device whose
 // stream-K grid needs more CTAs than kNoallocSlots is rejected with
 // KEBAB_ENOTSUP. Host code cannot use the array's name as a device address,
-// so the first call on each device (with that device current) looks the
-// address up with cudaGetSymbolAddress and keeps it; make that first call
-// before any stream capture. Every call shares the one array: the flags are
-// cleared on the stream at the start of each call (cudaMemsetAsync, which
-// allocates nothing) and the partials are fully rewritten before they are
-// read, so calls that overlap on the GPU (different streams, or concurrent
-// host threads) race and must be serialised by the caller.
+// so a per-device set-up (with that device current) looks the address up with
+// cudaGetSymbolAddress and keeps it. The set-up is also the moment the CUDA
+// driver loads this file's module onto the device (lazy module loading), which
+// is when the 20 MiB array and the kernels' code are committed: it is the one
+// step that may allocate. It runs on the first call per device, or explicitly
+// with a set-up-only call (null pointers and M = N = K = 0); make that call
+// before entering the code that must not allocate, and before any stream
+// capture. Every call shares the one array: the flags are cleared on the
+// stream at the start of each call (cudaMemsetAsync, which allocates nothing)
+// and the partials are fully rewritten before they are read, so calls that
+// overlap on the GPU (different streams, or concurrent host threads) race and
+// must be serialised by the caller.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -53,43 +58,64 @@ std::mutex g_noalloc_mu;
 NoallocDevice g_noalloc_dev[64];
 
 template <typename T>
-int launch_noalloc(const GemmProblem& p) {
+cudaError_t opt_in(int sm_count, int* max_clusters) {
   using L = UmmaSmem<kNoallocBN, kNoallocStages, 2>;
   auto kern = gemm_umma_ws_kernel<T, kNoallocBN, kNoallocStages, 2, true, 0, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t qc = {};
+  qc.gridDim = dim3(2 * (sm_count / 2), 1, 1);
+  qc.blockDim = dim3(UmmaEpi<kNoallocBN>::THREADS, 1, 1);
+  qc.dynamicSmemBytes = L::ALLOC;
+  cudaLaunchAttribute qa[1];
+  qa[0].id = cudaLaunchAttributeClusterDimension;
+  qa[0].val.clusterDim.x = 2;
+  qa[0].val.clusterDim.y = 1;
+  qa[0].val.clusterDim.z = 1;
+  qc.attrs = qa;
+  qc.numAttrs = 1;
+  int n = 0;
+  e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
+  (void)cudaGetLastError();
+  *max_clusters = std::min(sm_count / 2, (e == cudaSuccess && n > 0) ? n : sm_count / 2);
+  return cudaSuccess;
+}
+
+// Once per device, with that device current: the device address of the
+// static scratch, both dtypes' shared-memory opt-in (which also loads their
+// code) and the pair count. Everything a later call needs, so later calls
+// allocate nothing.
+int setup_device(NoallocDevice** out) {
   DeviceInfo* dev = nullptr;
   int rc = device_info(&dev);
   if (rc) return rc;
   if (dev->device >= 64) return fail(KEBAB_ENOTSUP, "no-alloc GEMM supports device ids below 64");
   NoallocDevice& nd = g_noalloc_dev[dev->device];
-  {
-    // Once per device, with that device current: the device address of the
-    // static scratch, the kernel's shared-memory opt-in and the pair count.
-    std::lock_guard<std::mutex> lk(g_noalloc_mu);
-    if (!nd.ready) {
-      void* ptr = nullptr;
-      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
-      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
-      if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
-      cudaLaunchConfig_t qc = {};
-      qc.gridDim = dim3(2 * (dev->sm_count / 2), 1, 1);
-      qc.blockDim = dim3(UmmaEpi<kNoallocBN>::THREADS, 1, 1);
-      qc.dynamicSmemBytes = L::ALLOC;
-      cudaLaunchAttribute qa[1];
-      qa[0].id = cudaLaunchAttributeClusterDimension;
-      qa[0].val.clusterDim.x = 2;
-      qa[0].val.clusterDim.y = 1;
-      qa[0].val.clusterDim.z = 1;
-      qc.attrs = qa;
-      qc.numAttrs = 1;
-      int n = 0;
-      e = cudaOccupancyMaxActiveClusters(&n, kern, &qc);
-      (void)cudaGetLastError();
-      nd.max_clusters = std::min(dev->sm_count / 2, (e == cudaSuccess && n > 0) ? n : dev->sm_count / 2);
-      nd.scratch = static_cast<NoallocScratch*>(ptr);
-      nd.ready = true;
-    }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!nd.ready) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(no-alloc scratch)");
+    int c16 = 0, c_bf16 = 0;
+    if ((e = opt_in<__half>(dev->sm_count, &c16)) != cudaSuccess ||
+        (e = opt_in<__nv_bfloat16>(dev->sm_count, &c_bf16)) != cudaSuccess)
+      return cuda_fail(e, "cudaFuncSetAttribute(no-alloc stream-K kernel)");
+    nd.max_clusters = std::min(c16, c_bf16);
+    nd.scratch = static_cast<NoallocScratch*>(ptr);
+    nd.ready = true;
   }
+  *out = &nd;
+  return KEBAB_OK;
+}
+
+template <typename T>
+int launch_noalloc(const GemmProblem& p) {
+  using L = UmmaSmem<kNoallocBN, kNoallocStages, 2>;
+  auto kern = gemm_umma_ws_kernel<T, kNoallocBN, kNoallocStages, 2, true, 0, true>;
+  NoallocDevice* ndp = nullptr;
+  int rc = setup_device(&ndp);
+  if (rc) return rc;
+  NoallocDevice& nd = *ndp;
   const int clusters = nd.max_clusters;
   if (2 * clusters > kNoallocSlots)
     return fail(KEBAB_ENOTSUP, "no-alloc GEMM: this device needs " + std::to_string(2 * clusters) +
@@ -151,12 +177,26 @@ int launch_noalloc(const GemmProblem& p) {
 }
 
 }  // namespace
+
+// Called by kebab_shutdown(): forget every device's set-up, so a call after a
+// device reset looks the address up and opts in again.
+void noalloc_reset() {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  for (auto& d : g_noalloc_dev) d = NoallocDevice();
+}
+
 }  // namespace kb
 
 using namespace kb;
 
 extern "C" int kebab_gemm_streamk_noalloc(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M,
                                           int64_t N, int64_t K, kebab_stream_t stream) {
+  if (!A && !B && !C && M == 0 && N == 0 && K == 0) {
+    // Set-up only: the per-device step that may allocate (see above).
+    NoallocDevice* nd = nullptr;
+    (void)stream;
+    return setup_device(&nd);
+  }
   if (!A || !B || !C) return fail(KEBAB_EINVAL, "null pointer passed to kebab_gemm_streamk_noalloc");
   if (M <= 0 || N <= 0 || K <= 0) return fail(KEBAB_EINVAL, "invalid dimensions");
   if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "no-alloc GEMM supports F16 and BF16");

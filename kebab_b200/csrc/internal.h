@@ -77,6 +77,9 @@ int launch_v110_persistent_n128(const GemmProblem& p);
 int launch_v111_persistent_n64(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
+// Forgets the no-alloc GEMM's per-device set-up (kebab_shutdown()).
+void noalloc_reset();
+
 // Validation shared by the TMA-based rungs: 16-byte aligned pointers and
 // 16-byte row pitches of A, B and C in their storage layouts (RC: K % 8 and
 // M % 8; a column-major A needs M % 8, a row-major B or C needs N % 8).

@@ -309,6 +309,7 @@ int kebab_probe_wait_timeout(kebab_stream_t stream, uint64_t timeout_us) {
 }
 
 void kebab_shutdown(void) {
+  noalloc_reset();
   {
     std::lock_guard<std::mutex> lk(g_tmap_mu);
     g_tmaps.clear();

@@ -100,9 +100,16 @@ def broadcast_gemm_pipelined(A_shard, B, C_shard=None, chunks=4, src=0, version=
     multi = dist.is_initialized() and dist.get_world_size(group) > 1
     works = [dist.broadcast(B[n0:n1], src=src, group=group, async_op=True) if multi else None
              for n0, n1 in bounds]
+    run_stream = stream if stream is not None else (torch.cuda.current_stream() if B.is_cuda else None)
     for (n0, n1), w in zip(bounds, works):
         if w is not None:
-            w.wait()
+            # Work.wait() orders only the current stream after the broadcast;
+            # the chunk's GEMM runs on `run_stream`, so make that one wait.
+            if run_stream is not None:
+                with torch.cuda.stream(run_stream):
+                    w.wait()
+            else:
+                w.wait()
         out = sharded_gemm(A_shard, B[n0:n1], C_shard[n0:n1], version=version, gemm_fn=gemm_fn, stream=stream)
         if out is not None and out.data_ptr() != C_shard[n0:n1].data_ptr():
             C_shard[n0:n1].copy_(out)

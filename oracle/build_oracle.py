@@ -8,8 +8,9 @@ Outputs:
   oracle/_ref/libkebab_ref_sparse_mma.so  sparse_mma.cu host encoders
 
 The oracle/_ref libraries are built only where the reference tree exists
-(KEBAB_REFERENCE_ROOT, default the mounted reference); on a machine without
-it, previously built files are used as they are.
+(KEBAB_REFERENCE_ROOT, else a checkout named `reference` beside this
+repository's directory, i.e. ../reference from the repository root); on a
+machine without it, previously built files are used as they are.
 """
 import os
 import shutil
@@ -17,7 +18,7 @@ import subprocess
 import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_ROOT = os.environ.get("KEBAB_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("KEBAB_REFERENCE_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 

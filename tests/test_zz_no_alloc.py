@@ -1,17 +1,23 @@
 """kebab_gemm_streamk_noalloc — the stream-K GEMM for callers that cannot
 allocate device memory (allocator callbacks, fixed-budget serving loops,
-plugin hosts that forbid cudaMalloc after start-up). Its output must match
-the regular entry point (kebab_gemm, rung 109, which allocates its stream-K
-workspace) within the north-star tolerance, on two calls in a row: the
-static scratch keeps the previous call's contents, so the second call checks
-that nothing stale leaks in. Collected last so that a run stopping at the
-first failure has already run every other test."""
+plugin hosts that forbid cudaMalloc after start-up).
+
+It runs the same kernel instantiation with the same work split and the same
+fixed-order fix-up as the regular entry point's rung 109 (which allocates its
+stream-K workspace), so the two outputs must be identical bit for bit, on two
+calls in a row: the static scratch keeps the previous call's contents, so the
+second call checks that nothing stale leaks in. Each output is also checked
+against the CPU oracle under the north-star tolerance, and, once the per-device
+set-up call has been made, further calls (new shapes, a new stream) must leave
+the device's free memory unchanged. Collected last so that a run stopping at
+the first failure has already run every other test."""
 import ctypes
 
 import numpy as np
 import pytest
 
 import oracle as O
+from gemm_util import assert_close, inputs, to_device
 
 pytestmark = pytest.mark.gpu
 
@@ -26,18 +32,28 @@ def _noalloc():
     return f
 
 
-@pytest.mark.parametrize("shape,dtype", [((4096, 4096, 1024), 0), ((2048, 3072, 512), 1), ((512, 768, 256), 0)])
+def _oracle_sample(A_bits, B_bits, M, N, K, dtype, rng, n=4096):
+    """Oracle values at n random elements plus every element of 8 random rows."""
+    rows = rng.integers(0, M, 8)
+    ii = np.concatenate([rng.integers(0, M, n), np.repeat(rows, N)])
+    jj = np.concatenate([rng.integers(0, N, n), np.tile(np.arange(N), rows.size)])
+    return ii, jj, O.gemm_elems(A_bits, B_bits, ii, jj, M, N, K, dtype)
+
+
+@pytest.mark.parametrize("shape,dtype", [((4096, 4096, 1024), O.F16), ((2048, 3072, 512), O.BF16),
+                                         ((512, 768, 256), O.F16)])
 def test_noalloc_matches_regular_entry_point(cuda, shape, dtype):
     import torch
     import kebab_b200 as kb
     M, N, K = shape
-    td = torch.float16 if dtype == 0 else torch.bfloat16
+    td = torch.float16 if dtype == O.F16 else torch.bfloat16
     stream = torch.cuda.current_stream().cuda_stream
     f = _noalloc()
-    g = torch.Generator(device=cuda).manual_seed(M + N + K)
+    rng = np.random.default_rng(M + N + K)
     for call in range(2):  # two calls in a row, different inputs
-        A = (torch.randn((M, K), generator=g, device=cuda) / K ** 0.5).to(td)
-        B = (torch.randn((N, K), generator=g, device=cuda) / K ** 0.5).to(td)
+        A_bits, B_bits = inputs(M, N, K, seed=1000 * call + M, dtype=dtype)
+        A = to_device(A_bits, (M, K), dtype, cuda)
+        B = to_device(B_bits, (N, K), dtype, cuda)
         ref = torch.full((N, M), float("nan"), dtype=td, device=cuda)
         out = torch.full((N, M), float("nan"), dtype=td, device=cuda)
         assert kb.gemm_raw(dtype, A.data_ptr(), B.data_ptr(), ref.data_ptr(), M, N, K, "RC", 109, stream) == kb.OK
@@ -45,9 +61,35 @@ def test_noalloc_matches_regular_entry_point(cuda, shape, dtype):
         assert rc == kb.OK, kb.last_error()
         torch.cuda.synchronize()
         assert kb.device_status()[0] == kb.OK
-        ok, rel, worst = O.check_tolerance(out.float().cpu().numpy().reshape(-1),
-                                           ref.float().cpu().numpy().reshape(-1))
-        assert ok, "call %d: rel_fro=%.3e worst=%.3f" % (call, rel, worst)
+        o = out.float().cpu().numpy()  # [N, M]: column-major C
+        r = ref.float().cpu().numpy()
+        assert np.array_equal(o, r), "call %d: %d elements differ from rung 109" % (call, int((o != r).sum()))
+        ii, jj, want = _oracle_sample(A_bits, B_bits, M, N, K, dtype, rng)
+        assert_close(o[jj, ii], want, "no-alloc call %d vs oracle" % call, dtype)
+
+
+def test_noalloc_allocates_nothing_after_setup(cuda):
+    """After the set-up-only call (null pointers, M = N = K = 0), calls on new
+    shapes and on a new stream leave the device's free memory unchanged."""
+    import torch
+    import kebab_b200 as kb
+    f = _noalloc()
+    assert f(O.F16, None, None, None, 0, 0, 0, None) == kb.OK, kb.last_error()
+    shapes = [(1024, 2048, 512, O.F16), (768, 512, 1024, O.BF16), (2048, 2048, 256, O.F16)]
+    bufs = []
+    for M, N, K, dt in shapes:
+        td = torch.float16 if dt == O.F16 else torch.bfloat16
+        bufs.append((torch.randn((M, K), device=cuda).to(td), torch.randn((N, K), device=cuda).to(td),
+                     torch.empty((N, M), dtype=td, device=cuda), M, N, K, dt))
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    for A, B, C, M, N, K, dt in bufs:
+        assert f(dt, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, s.cuda_stream) == kb.OK, kb.last_error()
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    assert free1 == free0, "free device memory changed by %d bytes" % (free0 - free1)
+    assert kb.device_status()[0] == kb.OK
 
 
 def test_noalloc_rejects_bad_arguments(cuda):
