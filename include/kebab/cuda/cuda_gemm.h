@@ -50,4 +50,42 @@ KEBAB_DECLARE_RUNG(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64)   
 KEBAB_DECLARE_RUNG(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c)  // v105, row-major C
 #undef KEBAB_DECLARE_RUNG
 
+// The reference's own launcher names (kebab/include/kebab/cuda/cuda_gemm.h:43-257,
+// every non-template fp16 / bf16 launcher; the gemm_v2 template is left out),
+// each forwarding to the B200 rung its version id maps to (kebab_version_name()
+// tells which), with the same (A, B, C, M, N, K, lhs_format, rhs_format,
+// stream) arguments.
+#define KEBAB_REFERENCE_ALIAS_F16(NAME, ID)                                                              \
+  void NAME(const __half* A, const __half* B, __half* C, int M, int N, int K, char lhs_format,          \
+            char rhs_format, cudaStream_t stream);
+#define KEBAB_REFERENCE_ALIAS_BF16(NAME, ID)                                                             \
+  void NAME(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,       \
+            char lhs_format, char rhs_format, cudaStream_t stream);
+#define KEBAB_REFERENCE_ALIASES \
+  KEBAB_REFERENCE_ALIAS_BF16(gemm_v1_warptiling_bf16_baseline, 1) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v1_warptiling_fp16_baseline, 1) \
+  KEBAB_REFERENCE_ALIAS_BF16(gemm_v3_wgmma_tma_warpgroup_bf16, 3) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v3_wgmma_tma_warpgroup_fp16, 3) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v4_wgmma_tma_warpgroup_warpspecialized_fp16, 4) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v5_wgmma_tma_warpgroup_warpspecialized_persistent_fp16, 5) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v6_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_fp16, 6) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v7_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_fp16, 7) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v8_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_fp16, 8) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v9_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_streamstore_fp16, 9) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v10_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_fp16, 10) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v11_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_fp16, 11) \
+  KEBAB_REFERENCE_ALIAS_BF16(gemm_v12_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_stmatrix_padded_bf16, 12) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v12_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_stmatrix_padded_fp16, 12) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v13_wgmma_tma_warpspecialized_persistent_tilescheduler_ptxbarrier_tma2d_fp16, 13) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v14_wgmma_tma_warpspecialized_persistent_ptxbarrier_tmastore_hilbert_stmatrix_padded_nocluster_fp16, 14) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v15_wgmma_tma_warpspecialized_ptxbarrier_tmastore_hilbert_stmatrix_padded_nocluster_nopersistent_fp16, 15) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v16_wgmma_tma_warpspecialized_persistent_ptxbarrier_tmastore_hilbert_stmatrix_padded_nocluster_linearschedule_fp16, 16) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v17_wgmma_tma_warpgroup_ptxbarrier_fp16, 17) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v18_wgmma_tma_warpgroup_warpspecialized_persistent_stmatrix_fp16, 18) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v19_wgmma_tma_warpgroup_warpspecialized_persistent_hilbert_fp16, 19) \
+  KEBAB_REFERENCE_ALIAS_F16(gemm_v41_wgmma_tma_warpgroup_warpspecialized_fp16, 41)
+KEBAB_REFERENCE_ALIASES
+#undef KEBAB_REFERENCE_ALIAS_F16
+#undef KEBAB_REFERENCE_ALIAS_BF16
+
 }  // namespace baseline

@@ -243,6 +243,23 @@ KEBAB_RUNG_LAUNCHER(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64, 1
 KEBAB_RUNG_LAUNCHER(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c, 141)
 #undef KEBAB_RUNG_LAUNCHER
 
+// The reference's launcher names, forwarding to the rung their id maps to.
+#define KEBAB_REFERENCE_ALIAS_F16(NAME, ID)                                                              \
+  void NAME(const __half* A, const __half* B, __half* C, int M, int N, int K, char lhs_format,          \
+            char rhs_format, cudaStream_t stream) {                                                     \
+    const char mode[3] = {lhs_format, rhs_format, 0};                                                   \
+    report(kebab_gemm(KEBAB_F16, A, B, C, M, N, K, mode, ID, stream), #NAME);                           \
+  }
+#define KEBAB_REFERENCE_ALIAS_BF16(NAME, ID)                                                             \
+  void NAME(const __nv_bfloat16* A, const __nv_bfloat16* B, __nv_bfloat16* C, int M, int N, int K,       \
+            char lhs_format, char rhs_format, cudaStream_t stream) {                                    \
+    const char mode[3] = {lhs_format, rhs_format, 0};                                                   \
+    report(kebab_gemm(KEBAB_BF16, A, B, C, M, N, K, mode, ID, stream), #NAME);                          \
+  }
+KEBAB_REFERENCE_ALIASES
+#undef KEBAB_REFERENCE_ALIAS_F16
+#undef KEBAB_REFERENCE_ALIAS_BF16
+
 }  // namespace baseline
 
 // ---------------------------------------------------------------------------

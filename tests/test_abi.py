@@ -48,6 +48,19 @@ def test_cpp_mirror_symbols_exported():
     assert "baseline::gemm_cuda_version_feature_name(int)" in out
 
 
+def test_reference_launcher_aliases_exported():
+    """The reference's own launcher names (its cuda_gemm.h:43-257) are exported
+    with their reference argument types, and each id maps to a real rung."""
+    out = subprocess.run(["nm", "-DC", kb.LIB_PATH], capture_output=True, text=True).stdout
+    src = open(os.path.join(INC, "kebab", "cuda", "cuda_gemm.h")).read()
+    aliases = re.findall(r"KEBAB_REFERENCE_ALIAS_(F16|BF16)\((gemm_\w+), (\d+)\)", src)
+    assert len(aliases) == 22
+    for dt, name, vid in aliases:
+        elem = "__half" if dt == "F16" else "__nv_bfloat16"
+        assert "baseline::%s(%s const*" % (name, elem) in out, name
+        assert kb.version_name(int(vid)) != "unknown", name
+
+
 def test_null_and_dims_rejected():
     L = kb.lib()
     assert L.kebab_gemm(kb.F16, None, None, None, 8, 8, 8, b"RC", 104, None) == kb.EINVAL
