@@ -61,6 +61,9 @@ def parse():
                    help="N-chunks of the pipelined broadcast + GEMM measurement (N > 1 GPUs)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-cublas", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the other BASELINE configs (C2 2048/4096, C4a, C4b, C5 at N=1; C3 strong and C4a "
+                        "at every N); they run by default with the default headline workload")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work for the cpu_baseline sample")
     return p.parse_args()
 
@@ -151,6 +154,10 @@ class ClockSampler:
         if watts:
             out["power_w"] = float(np.median(watts))
         return out
+
+
+def kb_sm_count(torch, local):
+    return torch.cuda.get_device_properties(local).multi_processor_count
 
 
 def cpu_threads():
@@ -302,6 +309,320 @@ def run_reference(args, rank, world):
     }))
 
 
+# ----------------------------------------------------------------------------
+# Per-config extras: the other BASELINE configurations, each timed on the
+# device (one event pair around back-to-back launches, max over ranks), with a
+# sampled check of this rank's output against the CPU oracle outside the
+# timed region, the SM clock of the last timed launch read from the kernel's
+# own clock probe, and cuBLAS in the same loop on rank 0 at N = 1.
+# ----------------------------------------------------------------------------
+DENSE_FLOP_PER_CLK_SM = 8192.0  # tcgen05 kind::f16, measured (microbench)
+
+
+def _round_bf16(c):
+    u = np.asarray(c, np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return (u.astype(np.uint32) << 16).view(np.float32)
+
+
+def sample_parity(torch, A, B, C, bf16, seed, rows=3, row_cols=1024, elems=4096, threads=1):
+    """Checks a seeded sample of C ([N, M] column-major tensor = A [M, K] * B
+    [N, K]^T) against the oracle restatement of the reference CPU GEMM: the
+    first, the last and one random row over `row_cols` consecutive columns,
+    plus `elems` random elements. Tolerance: relative Frobenius <= 1e-3 and
+    |d| <= 1e-2 (1 + |ref|) per element; for BF16 output against the oracle
+    rounded to BF16, with the raw distance to the FP32 oracle under 4e-3."""
+    import oracle as O
+    M, K = A.shape
+    N = B.shape[0]
+    g = np.random.default_rng(seed)
+    rs = np.unique(np.array([0, M - 1, int(g.integers(0, M))]))[:rows]
+    c0 = int(g.integers(0, max(1, N - row_cols + 1)))
+    cols = np.arange(c0, min(N, c0 + row_cols))
+    ii = np.concatenate([g.integers(0, M, elems), np.repeat(rs, cols.size)]).astype(np.int64)
+    jj = np.concatenate([g.integers(0, N, elems), np.tile(cols, rs.size)]).astype(np.int64)
+    ur, ir = np.unique(ii, return_inverse=True)
+    uc, ic = np.unique(jj, return_inverse=True)
+    dev = A.device
+
+    def bits(t, idx):
+        sub = t[torch.from_numpy(idx).to(dev)].contiguous()
+        return sub.view(torch.int16).cpu().numpy().view(np.uint16).reshape(-1)
+
+    Ah, Bh = bits(A, ur), bits(B, uc)
+    got = C[torch.from_numpy(jj).to(dev), torch.from_numpy(ii).to(dev)].float().cpu().numpy()
+    dt = O.BF16 if bf16 else O.F16
+    want = O.gemm_elems(Ah, Bh, ir.astype(np.int64), ic.astype(np.int64), ur.size, uc.size, K, dt, threads)
+    out = {"elements": int(ii.size)}
+    ok = True
+    if bf16:
+        ok_raw, rel_raw, _ = O.check_tolerance(got, want, 4e-3, 1e-2)
+        out["rel_fro_raw"] = rel_raw
+        ok = ok and ok_raw
+        want = _round_bf16(want)
+    ok2, rel, worst = O.check_tolerance(got, want, 1e-3, 1e-2)
+    out.update({"ok": bool(ok and ok2), "rel_fro": rel, "worst_elem_ratio": worst})
+    return out
+
+
+class Extras:
+    def __init__(self, torch, dist, kb, rank, world, device, stream, sm_count, cublas):
+        self.torch, self.dist, self.kb = torch, dist, kb
+        self.rank, self.world, self.device, self.stream = rank, world, device, stream
+        self.sm_count = sm_count
+        self.cublas = cublas and rank == 0 and world == 1
+        self.threads = max(1, cpu_threads() // max(1, world))
+
+    def sync(self):
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize()
+
+    def max_over_ranks(self, v):
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], device=self.device, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def all_true(self, ok):
+        if self.world == 1:
+            return bool(ok)
+        t = self.torch.tensor([0.0 if ok else 1.0], device=self.device, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.item() == 0.0
+
+    def loop_ms(self, fn, steps, warmup, probe=True):
+        """Device ms of `steps` back-to-back calls (one event pair, max over
+        ranks) and the time-weighted SM clock of all of them (clock probe)."""
+        torch = self.torch
+        for i in range(warmup):
+            fn(i)
+        probe_buf = torch.zeros((steps, 256, 4), dtype=torch.int64, device=self.device) if probe else None
+        self.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for i in range(steps):
+            if probe:
+                self.kb.clock_probe(probe_buf[i])  # each launch records its own SM clock
+            fn(i)
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        self.kb.clock_probe(None)
+        rc, code = self.kb.device_status()
+        if rc != self.kb.OK:
+            raise RuntimeError("device status 0x%x" % code)
+        ms = self.max_over_ranks(e0.elapsed_time(e1))
+        clk = self.kb.clock_probe_mhz(probe_buf) if probe else None
+        return ms, clk
+
+    def cublas_ms(self, As, Bs, steps, warmup):
+        torch = self.torch
+        torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+        torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+        n = len(As)
+        for i in range(warmup):
+            torch.matmul(As[i % n], Bs[i % n].t())
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        for i in range(steps):
+            torch.matmul(As[i % n], Bs[i % n].t())
+        e1.record(self.stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def inputs(self, M, N, K, dtype, seed, a_std=None, b_std=None):
+        torch = self.torch
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed)
+        a_std = 1.0 / np.sqrt(K) if a_std is None else a_std
+        b_std = 1.0 / np.sqrt(K) if b_std is None else b_std
+        A = torch.empty((M, K), dtype=dtype, device=self.device)
+        B = torch.empty((N, K), dtype=dtype, device=self.device)
+        for T, std in ((A, a_std), (B, b_std)):  # in row slabs: no 4-byte temporary of the whole operand
+            step = max(1, (1 << 28) // (4 * K))
+            for r0 in range(0, T.shape[0], step):
+                r1 = min(T.shape[0], r0 + step)
+                T[r0:r1] = (torch.randn((r1 - r0, K), generator=g, device=self.device) * std).to(dtype)
+        return A, B
+
+    def clock_fields(self, tflops, clk, sparse=False):
+        if not clk:
+            return {}
+        peak = self.sm_count * DENSE_FLOP_PER_CLK_SM * (2.0 if sparse else 1.0) * clk["sm_mhz"] * 1e6 / 1e12
+        return {"effective_sm_mhz": clk["sm_mhz"], "frac_of_clock_peak": tflops / peak,
+                "clock_peak_tflops": peak, "probe": clk}
+
+    def dense(self, name, M_global, N, K, bf16, sets, steps, warmup, version=120, a_std=None, b_std=None,
+              sharded=True, bcast_b=False):
+        """A dense config, M-sharded over the ranks (rank r owns a row block);
+        with bcast_b, B of the first input set is broadcast from rank 0 first,
+        so every rank multiplies by the same B."""
+        torch, kb = self.torch, self.kb
+        dtype = torch.bfloat16 if bf16 else torch.float16
+        code = kb.BF16 if bf16 else kb.F16
+        M = M_global // self.world if sharded else M_global
+        data = []
+        for s in range(sets):
+            A, B = self.inputs(M, N, K, dtype, 7919 * s + 31 * self.rank + M_global, a_std, b_std)
+            data.append((A, B, torch.empty((N, M), dtype=dtype, device=self.device)))
+        if bcast_b and self.world > 1:
+            self.dist.broadcast(data[0][1], src=0)  # also sets up NCCL for the large broadcasts below
+            self.sync()
+        sp = self.stream.cuda_stream
+
+        def step(i):
+            A, B, C = data[i % sets]
+            rc = kb.gemm_raw(code, A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, "RC", version, sp)
+            if rc != kb.OK:
+                raise kb.KebabError(rc, kb.last_error())
+
+        ms, clk = self.loop_ms(step, steps, warmup)
+        per = ms / steps
+        flops = 2.0 * M_global * N * K if sharded else 2.0 * M * N * K * self.world
+        tflops = flops / (per * 1e-3) / 1e12
+        rung = kb.lib().kebab_resolve_version(version, code, M, N, K)
+        out = {"workload": name, "M": M_global, "N": N, "K": K, "M_per_rank": M, "dtype": "bf16" if bf16 else "fp16",
+               "rung": rung, "rung_name": kb.version_name(rung), "launches": steps, "input_sets": sets,
+               "ms_per_gemm": per, "tflops": tflops}
+        out.update(self.clock_fields(tflops / self.world, clk))
+        if self.cublas:
+            cb = self.cublas_ms([d[0] for d in data], [d[1] for d in data], steps, warmup)
+            out["cublas_tflops"] = 2.0 * M * N * K / (cb * 1e-3) / 1e12
+            out["vs_cublas"] = tflops / out["cublas_tflops"]
+        A, B, C = data[0]
+        step(0)
+        torch.cuda.synchronize()
+        par = sample_parity(torch, A, B, C, bf16, seed=M_global + N + self.rank, threads=self.threads)
+        out["parity"] = par
+        out["parity_all_ranks"] = self.all_true(par["ok"])
+        return out, data
+
+    def hbm(self, out, M, N, K):
+        """Roofline of an HBM-bound config: algorithmic bytes (A + B read, C
+        written once) over the measured launch time."""
+        nbytes = 2.0 * (M * K + N * K + M * N)
+        gbs = nbytes / (out["ms_per_gemm"] * 1e-3) / 1e9
+        peaks = load_peaks()
+        out.update({"algorithmic_bytes": nbytes, "gbs": gbs, "hbm_peak_gbs": peaks["hbm_gbs"],
+                    "frac_of_hbm": gbs / peaks["hbm_gbs"], "frac_of_8tbs": gbs / 8000.0})
+        if "cublas_tflops" in out:
+            out["cublas_gbs"] = nbytes / (2.0 * M * N * K / (out["cublas_tflops"] * 1e12)) / 1e9
+        return out
+
+    def c3_strong(self, steps=5, warmup=2):
+        """32768^3 BF16 split into M row blocks; B (2 GiB)
+        broadcast from rank 0. GEMM-only time, the broadcast alone, and
+        broadcast followed by the GEMM, each device-timed, max over ranks."""
+        torch, dist = self.torch, self.dist
+        S = 32768
+        out, data = self.dense("c3_strong_bf16_32768", S, S, S, True, 1, steps, warmup, bcast_b=True)
+        A, B, C = data[0]
+        out["scaling"] = "strong"
+        if self.world > 1:
+
+            def one(with_gemm):
+                self.sync()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+                dist.broadcast(B, src=0)
+                if with_gemm:
+                    self.kb.gemm(A, B, C, version=120, stream=self.stream)
+                e1.record(self.stream)
+                torch.cuda.synchronize()
+                return self.max_over_ranks(e0.elapsed_time(e1))
+
+            out["broadcast_ms"] = sorted(one(False) for _ in range(3))[1]
+            out["broadcast_gbs"] = 2.0 * S * S / (out["broadcast_ms"] * 1e-3) / 1e9
+            out["broadcast_plus_gemm_ms"] = sorted(one(True) for _ in range(3))[1]
+            out["broadcast_plus_gemm_tflops"] = 2.0 * S ** 3 / (out["broadcast_plus_gemm_ms"] * 1e-3) / 1e12
+        else:
+            out["broadcast_ms"] = 0.0
+            out["broadcast_plus_gemm_ms"] = out["ms_per_gemm"]
+            out["broadcast_plus_gemm_tflops"] = out["tflops"]
+        del data
+        return out
+
+    def sparse(self, M, N, K, sets, steps, warmup):
+        """A dense N(0,1) pruned 2:4 and compressed once
+        (timed separately: packer GB/s), B N(0,1)/sqrt(K); dense-equivalent
+        TFLOP/s (2MNK) against 2x the dense clock peak."""
+        torch, kb = self.torch, self.kb
+        data = []
+        packer = None
+        for s in range(sets):
+            A, B = self.inputs(M, N, K, torch.float16, 104729 * s + 5, a_std=1.0)
+            t0, t1, t2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            t0.record(self.stream)
+            pr = kb.sparse24_prune(A)
+            t1.record(self.stream)
+            pk, E = kb.sparse24_compress(pr)
+            t2.record(self.stream)
+            torch.cuda.synchronize()
+            if s == 0:
+                mk = M * K
+                packer = {"prune_gbs": 4.0 * mk / (t0.elapsed_time(t1) * 1e-3) / 1e9,
+                          "compress_gbs": (2.0 * mk + mk + mk / 8.0) / (t1.elapsed_time(t2) * 1e-3) / 1e9,
+                          "prune_ms": t0.elapsed_time(t1), "compress_ms": t1.elapsed_time(t2)}
+            del A
+            data.append((pr, pk, E, B, torch.empty((N, M), dtype=torch.float16, device=self.device)))
+        sp = self.stream.cuda_stream
+
+        def step(i):
+            pr, pk, E, B, C = data[i % sets]
+            rc = kb._sp().kebab_gemm_sparse24(kb.F16, pk.data_ptr(), E.data_ptr(), B.data_ptr(), C.data_ptr(),
+                                             M, N, K, sp)
+            if rc != kb.OK:
+                raise kb.KebabError(rc, kb.last_error())
+
+        ms, clk = self.loop_ms(step, steps, warmup)
+        per = ms / steps
+        tflops = 2.0 * M * N * K / (per * 1e-3) / 1e12
+        tm, tn = kb.sparse24_tile(M, N)
+        out = {"workload": "c5_sparse24_fp16_%d" % M, "M": M, "N": N, "K": K, "tile": [tm, tn], "launches": steps,
+               "input_sets": sets, "ms_per_gemm": per, "tflops_dense_equivalent": tflops,
+               "tflops_useful": tflops / 2.0, "packer": packer}
+        peaks = load_peaks()
+        out["frac_of_2x_burst_peak"] = tflops / (2.0 * peaks["bf16_tflops"])
+        out.update(self.clock_fields(tflops, clk, sparse=True))
+        if self.cublas:
+            cb = self.cublas_ms([d[0] for d in data], [d[3] for d in data], steps, warmup)
+            out["dense_cublas_tflops"] = 2.0 * M * N * K / (cb * 1e-3) / 1e12
+        pr, pk, E, B, C = data[0]
+        step(0)
+        torch.cuda.synchronize()
+        out["parity"] = sample_parity(torch, pr, B, C, False, seed=M + 5, threads=self.threads)
+        del data
+        return out
+
+
+def run_extras(args, torch, dist, kb, rank, world, device, stream, sm_count):
+    ex = Extras(torch, dist, kb, rank, world, device, stream, sm_count, cublas=not args.no_cublas)
+    out = {}
+    t0 = time.perf_counter()
+    if world == 1:
+        for n, sets, steps in ((2048, 10, 200), (4096, 3, 100)):
+            r, d = ex.dense("c2_fp16_%d" % n, n, n, n, False, sets, steps, 5, sharded=False)
+            del d
+            out["c2_%d" % n] = r
+        r, d = ex.dense("c4b_decode_fp16_64x8192x8192", 64, 8192, 8192, False, 3, 200, 5, a_std=1.0, b_std=0.02,
+                        sharded=False)
+        del d
+        out["c4b"] = ex.hbm(r, 64, 8192, 8192)
+        out["c5"] = ex.sparse(8192, 8192, 8192, 3, 100, 5)
+        torch.cuda.empty_cache()
+    r, d = ex.dense("c4a_prefill_fp16_16384x28672x8192", 16384, 28672, 8192, False, 1, 10, 3, a_std=1.0,
+                    b_std=0.02)
+    del d
+    out["c4a"] = r
+    torch.cuda.empty_cache()
+    out["c3_strong"] = ex.c3_strong()
+    torch.cuda.empty_cache()
+    out["extras_wall_s"] = time.perf_counter() - t0
+    return out
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -414,14 +735,20 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    # Every launch records its own SM clock (cycle counter / global timer per
+    # CTA): the time-weighted clock of the timed loop, not of its lead-in.
+    probe_buf = torch.zeros((args.steps, 256, 4), dtype=torch.int64, device=device)
     e_start.record(stream)
     for i in range(args.steps):
+        kb.clock_probe(probe_buf[i])
         step(i)
     e_end.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     clocks = sampler.stop()
+    kb.clock_probe(None)
+    probe_clk = kb.clock_probe_mhz(probe_buf)
     rc, code = kb.device_status()
     if rc != kb.OK:
         raise RuntimeError("device status 0x%x after timed steps" % code)
@@ -566,6 +893,27 @@ def main():
         cublas = {"value": flops_rank * n_cb / (c0.elapsed_time(c1) * 1e-3) / 1e12, "unit": UNIT, "clocks": cb_clocks,
                   "what": "torch.matmul (cuBLAS, FP32 accumulate) on the same inputs, 1 GPU, same number of back-to-back launches"}
 
+    # Headline parity: a seeded sample of this rank's C (input set 0) against
+    # the oracle, outside every timed region; verdicts gathered over ranks.
+    hp = sample_parity(torch, As[0], Bs[0], Cs[0], args.dtype == "bf16", seed=4242 + rank,
+                       threads=max(1, cpu_threads() // world))
+    t_ok = torch.tensor([0.0 if hp["ok"] else 1.0, hp["rel_fro"], hp["worst_elem_ratio"]], device=device,
+                        dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_ok, op=dist.ReduceOp.MAX)
+    parity = {"ok": t_ok[0].item() == 0.0, "rel_fro_max": t_ok[1].item(), "worst_elem_ratio_max": t_ok[2].item(),
+              "elements_per_rank": hp["elements"], "ranks": world,
+              "what": "first, last and one random row x 1024 columns plus 4096 random elements of each rank's C, "
+                      "against the oracle restatement of referenceGemmCpp<float>"}
+
+    extras = None
+    default_workload = (not args.strong and not sparse and (args.m, args.n, args.k) == (8192, 8192, 8192)
+                        and args.dtype == "fp16" and version == 120)
+    if default_workload and not args.no_extras:
+        del As, Bs, Cs, dA, dB, dC, hA, hB, hC, src_a
+        torch.cuda.empty_cache()
+        extras = run_extras(args, torch, dist, kb, rank, world, device, stream, kb_sm_count(torch, local))
+
     if rank != 0:
         if world > 1:
             dist.destroy_process_group()
@@ -601,6 +949,11 @@ def main():
                     "peak_kind": "%s HBM copy" % peaks["source"], "tflops": achieved,
                     "launch_ms_avg": avg_launch_ms,
                     "launch_ms_serialised_median": float(np.median(per_launch))}
+    if probe_clk:
+        sms = kb_sm_count(torch, local)
+        clk_peak = sms * DENSE_FLOP_PER_CLK_SM * (2.0 if sparse else 1.0) * probe_clk["sm_mhz"] * 1e6 / 1e12
+        roofline.update({"effective_sm_mhz": probe_clk["sm_mhz"], "frac_of_clock_peak": achieved / clk_peak,
+                         "clock_peak_tflops": clk_peak, "clock_probe": probe_clk})
     out = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
@@ -622,7 +975,10 @@ def main():
         "broadcast_ms": bcast_ms,
         "broadcast_gemm": bcast_gemm,
         "cublas": cublas,
+        "parity": parity,
     }
+    if extras:
+        out.update(extras)
     if sparse:
         out["metric"] = "2:4 sparse FP16 RC GEMM TFLOP/s (dense-equivalent 2MNK) @ M=N=K=8192"
         out["useful_tflops"] = value / 2.0

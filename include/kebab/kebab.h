@@ -83,6 +83,16 @@ int kebab_device_status(kebab_stream_t stream, uint32_t* code, int clear);
  * the KEBAB_WAIT_TIMEOUT_MS environment variable). */
 int kebab_set_wait_timeout_us(uint64_t timeout_us);
 
+/* Arms a clock probe for the next tcgen05 GEMM launch (dense rungs 103-111,
+ * 141, and the 2:4 sparse GEMM) made by this host thread: thread 0 of every
+ * CTA of that launch writes four uint64 at buf[4 * cta]: the SM cycle counter
+ * and the global nanosecond timer at entry, then both again at exit.
+ * Cycles / nanoseconds is the SM clock in GHz that CTA ran at. `buf` is a
+ * device buffer of 4 * max_ctas uint64; a launch with more CTAs than that
+ * leaves the probe armed and writes nothing. (NULL, 0) disarms. No
+ * reference counterpart: measurement support for the roofline. */
+int kebab_clock_probe(void* buf, int64_t max_ctas);
+
 /* Launches a one-warp kernel that waits on an mbarrier nobody arrives at,
  * with a budget of `timeout_us`; the wait expires and the kernel returns.
  * Exercises the timeout path without faulting or hanging the GPU. Returns

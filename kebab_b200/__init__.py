@@ -64,6 +64,8 @@ def lib():
         L.kebab_set_wait_timeout_us.restype = c.c_int
         L.kebab_probe_wait_timeout.argtypes = [c.c_void_p, c.c_uint64]
         L.kebab_probe_wait_timeout.restype = c.c_int
+        L.kebab_clock_probe.argtypes = [c.c_void_p, c.c_int64]
+        L.kebab_clock_probe.restype = c.c_int
         L.kebab_shutdown.argtypes = []
         L.kebab_shutdown.restype = None
         _lib = L
@@ -151,6 +153,43 @@ def device_status(stream=None, clear=True):
 
 def set_wait_timeout_us(us):
     check(lib().kebab_set_wait_timeout_us(us))
+
+
+def clock_probe(buf):
+    """Arms the clock probe for this thread's next tcgen05 GEMM launch: `buf`
+    is an int64 CUDA tensor of shape [ctas, 4] (None disarms)."""
+    if buf is None:
+        check(lib().kebab_clock_probe(None, 0))
+    else:
+        check(lib().kebab_clock_probe(ctypes.c_void_p(buf.data_ptr()), buf.shape[0]))
+
+
+def clock_probe_mhz(buf):
+    """SM clock (MHz) from clock-probe records: `buf` is [ctas, 4] (one
+    launch) or [launches, ctas, 4] (one launch per row, each armed with its
+    own slice). Per launch, the median over its CTAs of cycles and of
+    nanoseconds; over launches, total cycles / total nanoseconds, so the
+    figure is the time-weighted clock of the whole loop."""
+    import numpy as np
+    r = buf.cpu().numpy().astype(np.float64)
+    if r.ndim == 2:
+        r = r[None]
+    cyc, ns, ctas, mhz = 0.0, 0.0, 0, []
+    for rec in r:
+        rec = rec[(rec[:, 3] > rec[:, 1]) & (rec[:, 2] > rec[:, 0])]
+        if rec.shape[0] == 0:
+            continue
+        c = np.median(rec[:, 2] - rec[:, 0])
+        t = np.median(rec[:, 3] - rec[:, 1])
+        cyc += c
+        ns += t
+        ctas = max(ctas, rec.shape[0])
+        mhz.append(c / t * 1e3)
+    if ns == 0:
+        return None
+    return {"sm_mhz": cyc / ns * 1e3, "launches": len(mhz), "ctas": ctas,
+            "cta_us_median_per_launch": ns / len(mhz) / 1e3, "sm_mhz_min_launch": min(mhz),
+            "sm_mhz_max_launch": max(mhz)}
 
 
 def probe_wait_timeout(timeout_us=1000, stream=None):

@@ -19,6 +19,7 @@
 
 #include "internal.h"
 #include "kebab/cuda/cuda_gemm.h"
+#include "kebab/peer.h"
 
 namespace kb {
 namespace {
@@ -188,6 +189,24 @@ int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t
   const Rung* r = find_rung(id);
   GemmProblem p{(int)dtype, A, B, C, M, N, K, lhs, rhs, c_row, reinterpret_cast<cudaStream_t>(stream)};
   return r->launch(p);
+}
+
+int kebab_gemm_gated(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
+                     int version, const uint32_t* b_ready, int64_t chunk_cols, uint32_t epoch,
+                     kebab_stream_t stream) {
+  if (!A || !B || !C || !b_ready) return fail(KEBAB_EINVAL, "null pointer passed to kebab_gemm_gated");
+  if (M <= 0 || N <= 0 || K <= 0) return fail(KEBAB_EINVAL, "invalid dimensions");
+  if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "gated GEMM supports F16 and BF16");
+  const int id = resolve(version, M, N, K, true);
+  if (id < 0) return -id;
+  if (id != 104 && id != 105 && id != 107)
+    return fail(KEBAB_ENOTSUP, "gated B runs on the persistent rungs 104, 105 and 107; version " +
+                                   std::to_string(version) + " resolves to " + std::to_string(id));
+  GemmProblem p{(int)dtype, A, B, C, M, N, K, 'R', 'C', false, reinterpret_cast<cudaStream_t>(stream)};
+  p.b_ready = b_ready;
+  p.b_chunk_cols = chunk_cols;
+  p.b_epoch = epoch;
+  return find_rung(id)->launch(p);
 }
 
 }  // extern "C"

@@ -119,6 +119,8 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = (rank == 0);
   const WaitCtx& ctx = args.ctx;
+  ClockProbe probe;
+  probe.begin(args.clk);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -368,6 +370,7 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc<CG>(tmem_base, TMEM_COLS);
   }
+  probe.end(args.clk);
 }
 
 // E viewed as a 2-D array of uint16: 8 per 16-byte row, 128 rows per block.
@@ -444,6 +447,7 @@ int launch_sparse(int dtype, const void* Ap, const void* E, const void* B, void*
   cfg.attrs = attr;
   args.pdl = pdl_enabled() ? 1 : 0;
   cfg.numAttrs = args.pdl ? 2 : 1;
+  args.clk = take_clock_probe((int)cfg.gridDim.x);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tE, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_sparse launch");
   return KEBAB_OK;

@@ -162,8 +162,10 @@ struct UnitIter {
   }
 };
 
-// Bounded wait until a flag written by another CTA equals `want`.
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, const WaitCtx& ctx) {
+// Bounded wait until a flag written by another CTA (or by a stream memory
+// operation) equals `want`; `site` is recorded on expiry.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, const WaitCtx& ctx,
+                                          uint32_t site = SITE_PARTIAL) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
   if (v == want) return true;
@@ -175,7 +177,7 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t want, c
     if ((it & 63u) == 0u) {
       if (aborted(ctx.status)) return false;
       if (globaltimer() - t0 > ctx.timeout_ns) {
-        record_error(ctx.status, DEV_TIMEOUT, SITE_PARTIAL);
+        record_error(ctx.status, DEV_TIMEOUT, site);
         return false;
       }
     }
@@ -210,10 +212,19 @@ struct UmmaArgs {
   int l2_hint;              // 0: no hint; bits 0..1 policy of A, bits 2..3 of B (1 last, 2 first, 3 normal)
   int pdl = 0;              // launched with programmatic stream serialisation
   // Whole tiles: odd units of a CTA walk K from the end, so each wave starts
-  // on the K-blocks the previous wave read last (still in L2). Off by default:
-  // it ties a tile's summation order to its place in the schedule, so results
-  // would no longer match bit for bit between a single GPU and M-shards.
+  // on the K-blocks the previous wave read last (still in L2). It ties a
+  // tile's summation order to its place in the schedule, so results match
+  // between a single GPU and M-shards within tolerance, not bit for bit
+  // (KEBAB_SERPENTINE=0 restores bit-identity).
   int serp = 0;
+  unsigned long long* clk = nullptr;  // clock probe buffer (4 u64 per CTA) or null
+  // Gated B (non-null b_ready): B arrives in chunks of b_chunk_cols columns
+  // (a multiple of BN) while the kernel runs; chunk j may be read once
+  // b_ready[j] == b_epoch. Flags are raised in chunk order, so seeing chunk j
+  // ready implies every earlier chunk is.
+  const uint32_t* b_ready = nullptr;
+  int b_chunk_cols = 0;
+  uint32_t b_epoch = 0;
   WaitCtx ctx;
 };
 
@@ -287,6 +298,8 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   const uint32_t rank = (CG == 2) ? cluster_ctarank() : 0u;
   const bool leader = (rank == 0);
   const WaitCtx& ctx = args.ctx;
+  ClockProbe probe;
+  probe.begin(args.clk);
 
   if (threadIdx.x == 0) {
 #ifdef KEBAB_SK_TRACE
@@ -343,11 +356,23 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
       it.init(cluster_id, num_clusters, num_kb, args.dp_tiles, args.sk_tiles, SK, PERSISTENT, num_tiles);
       WorkUnit u;
       int pu = 0;
+      int chunk_seen = -1;  // gated B: highest chunk seen ready
       while (ok && it.next(u)) {
         int mb, nb;
         tile_coords(u.tile, args.tiles_m, args.tiles_n, args.group_m, mb, nb);
         const int m0 = mb * BM_T + (int)rank * 128;
         const int n0 = nb * BN + (int)rank * (BN / CG);
+        if (args.b_ready != nullptr) {
+          const int chunk = (nb * BN) / args.b_chunk_cols;
+          if (chunk > chunk_seen) {
+            if (!wait_flag(args.b_ready + chunk, args.b_epoch, ctx, SITE_BCHUNK)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            chunk_seen = chunk;
+          }
+        }
         const bool rev = !SK && args.serp && (pu++ & 1);
         for (int i = 0; i < u.k1 - u.k0; ++i) {
           const int kb = rev ? u.k1 - 1 - i : u.k0 + i;
@@ -651,6 +676,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc<CG>(tmem_base, TMEM_COLS);
   }
+  probe.end(args.clk);
 }
 
 }  // namespace kb

@@ -173,11 +173,26 @@ int launch_umma(const GemmProblem& p) {
   cfg.attrs = attr;
   args.pdl = pdl_enabled() ? 1 : 0;
   cfg.numAttrs = args.pdl ? 2 : 1;
+  // Serpentine K order (see UmmaArgs::serp): on unless KEBAB_SERPENTINE=0.
+  // It cuts DRAM reads (8192^3 on rung 107: 859 -> 725 MB per launch) at the
+  // price of M-sharded results matching a single GPU within tolerance rather
+  // than bit for bit.
   static const int serp_env = [] {
     const char* e = std::getenv("KEBAB_SERPENTINE");
-    return (e && *e) ? std::atoi(e) : 0;
+    return (e && *e) ? std::atoi(e) : 1;
   }();
   args.serp = serp_env;
+  if (p.b_ready != nullptr) {
+    if (!PERSISTENT || SK || (LAYOUT & LAYOUT_B_MN))
+      return fail(KEBAB_ENOTSUP, "gated B needs a persistent, non-stream-K rung with column-major B");
+    if (p.b_chunk_cols <= 0 || p.b_chunk_cols % BN != 0)
+      return fail(KEBAB_EINVAL, "gated B: chunk width " + std::to_string(p.b_chunk_cols) +
+                                    " must be a positive multiple of the rung's tile width " + std::to_string(BN));
+    args.b_ready = p.b_ready;
+    args.b_chunk_cols = (int)p.b_chunk_cols;
+    args.b_epoch = p.b_epoch;
+  }
+  args.clk = take_clock_probe((int)cfg.gridDim.x);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tC, args);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_umma_ws launch");
   return KEBAB_OK;

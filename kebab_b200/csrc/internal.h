@@ -60,6 +60,12 @@ struct GemmProblem {
   char lhs, rhs;  // 'R'/'C' storage of A and B
   bool c_row = false;  // C row-major (ldC = N) instead of column-major (ldC = M)
   cudaStream_t stream;
+  // Gated B (persistent tcgen05 rungs 104, 105, 107 only): B's columns arrive
+  // in chunks of b_chunk_cols while the GEMM runs; chunk j is readable once
+  // the device flag b_ready[j] equals b_epoch (see UmmaArgs).
+  const uint32_t* b_ready = nullptr;
+  int64_t b_chunk_cols = 0;
+  uint32_t b_epoch = 0;
 };
 
 // Launchers of the ladder rungs (return KEBAB_* status).
@@ -76,6 +82,11 @@ int launch_v109_pair_streamk(const GemmProblem& p);
 int launch_v110_persistent_n128(const GemmProblem& p);
 int launch_v111_persistent_n64(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
+
+// Clock probe armed by kebab_clock_probe() on this host thread for the next
+// tcgen05 GEMM launch: returns the buffer (and disarms it) when it holds at
+// least `ctas` CTAs' records, else null.
+unsigned long long* take_clock_probe(int ctas);
 
 // Forgets the no-alloc GEMM's per-device set-up (kebab_shutdown()).
 void noalloc_reset();

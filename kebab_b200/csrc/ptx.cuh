@@ -30,9 +30,35 @@ enum WaitSite : uint32_t {
   SITE_PROBE = 7,       // the deliberate-timeout probe kernel
   SITE_DRAIN = 8,       // teardown drain after an abort
   SITE_PARTIAL = 9,     // stream-K owner waiting for a contributor's partial
+  SITE_BCHUNK = 10,     // gated GEMM producer waiting for a chunk of B to arrive
 };
 
 // Where a kernel reports a failed wait, and how long a wait may take.
+// Clock probe: with a buffer given, thread 0 of every CTA records (SM cycle
+// counter, global ns timer) at entry and at exit, four u64 per CTA; the host
+// divides cycles by nanoseconds to get the SM clock the launch really ran at.
+struct ClockProbe {
+  unsigned long long c0 = 0, t0 = 0;
+  __device__ __forceinline__ void begin(unsigned long long* buf) {
+    if (buf && threadIdx.x == 0) {
+      asm volatile("mov.u64 %0, %%clock64;" : "=l"(c0));
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    }
+  }
+  __device__ __forceinline__ void end(unsigned long long* buf) const {
+    if (buf && threadIdx.x == 0) {
+      unsigned long long c1, t1;
+      asm volatile("mov.u64 %0, %%clock64;" : "=l"(c1));
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      unsigned long long* d = buf + (size_t)blockIdx.x * 4;
+      d[0] = c0;
+      d[1] = t0;
+      d[2] = c1;
+      d[3] = t1;
+    }
+  }
+};
+
 struct WaitCtx {
   uint32_t* status;     // device status word (see above)
   uint64_t timeout_ns;  // budget for any single barrier wait
@@ -262,6 +288,11 @@ __device__ __forceinline__ void tma_store_wait_read() {
 template <int N>
 __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
+}
+// Order this thread's earlier (acquire) observations of global memory before
+// its later async-proxy (TMA) reads of global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 // Make generic-proxy shared-memory writes visible to the async (TMA) proxy.
 __device__ __forceinline__ void fence_proxy_async_smem() {

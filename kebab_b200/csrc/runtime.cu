@@ -41,6 +41,19 @@ uint64_t default_timeout_ns() {
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
+namespace {
+thread_local unsigned long long* t_probe = nullptr;
+thread_local int64_t t_probe_ctas = 0;
+}  // namespace
+
+unsigned long long* take_clock_probe(int ctas) {
+  unsigned long long* p = t_probe;
+  if (!p || ctas > t_probe_ctas) return nullptr;
+  t_probe = nullptr;
+  t_probe_ctas = 0;
+  return p;
+}
+
 int fail(int code, const std::string& msg) {
   set_error(msg);
   return code;
@@ -262,6 +275,14 @@ using namespace kb;
 extern "C" {
 
 const char* kebab_last_error(void) { return t_last_error.c_str(); }
+
+int kebab_clock_probe(void* buf, int64_t max_ctas) {
+  if ((buf == nullptr) != (max_ctas == 0) || max_ctas < 0 || (reinterpret_cast<uintptr_t>(buf) & 7u))
+    return fail(KEBAB_EINVAL, "clock probe: need an 8-byte aligned buffer and a positive CTA count, or null and 0");
+  t_probe = static_cast<unsigned long long*>(buf);
+  t_probe_ctas = max_ctas;
+  return KEBAB_OK;
+}
 
 int kebab_set_wait_timeout_us(uint64_t timeout_us) {
   if (timeout_us == 0) return fail(KEBAB_EINVAL, "timeout must be positive");

@@ -80,9 +80,10 @@ def broadcast_gemm_pipelined(A_shard, B, C_shard=None, chunks=4, src=0, version=
     [n0, n1) of the [N, rows] C shard, also contiguous) starts as soon as
     chunk i has arrived, while later chunks are still in flight. On NCCL
     ranks the wait on a chunk is a stream dependency, not a host block.
-    Each element of C is computed from the same A row and B column in the
-    same K order as by sharded_gemm with a fixed rung, so the results match
-    it bit for bit. Returns C_shard.
+    Each element of C is computed from the same A row and B column as by
+    sharded_gemm; with the serpentine K order off (KEBAB_SERPENTINE=0) also
+    in the same K order, so the results match it bit for bit (by default
+    within tolerance). Returns C_shard.
 
     Measured on two B200s it is slower than broadcast-then-GEMM (32768^3
     BF16, 4 chunks: 37.4 ms against 29.1; 8192^3 FP16: 1.12 against 1.05):

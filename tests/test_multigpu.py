@@ -42,7 +42,8 @@ if rank == 0:
     full = kb.gemm(A, B, version=int(os.environ["KB_VERSION"]))
     torch.cuda.synchronize()
     same = torch.equal(full.view(torch.int16), Cg.view(torch.int16))
-    print("RESULT", "bitexact" if same else "mismatch", flush=True)
+    d = (full.float() - Cg.float()).norm() / full.float().norm()
+    print("RESULT", "bitexact" if same else "mismatch", "rel_fro=%.3e" % d.item(), flush=True)
 dist.barrier()
 dist.destroy_process_group()
 '''
@@ -56,8 +57,7 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("version,pipeline", [(104, ""), (105, ""), (105, "1")])
-def test_sharded_bitexact(cuda, version, pipeline):
+def _run(version, pipeline, serpentine):
     import torch
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
@@ -67,9 +67,27 @@ def test_sharded_bitexact(cuda, version, pipeline):
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
                    MASTER_PORT=str(port), KB_ROOT=ROOT, KB_VERSION=str(version), KB_PIPELINE=pipeline,
-                   NCCL_NVLS_ENABLE="0")
+                   NCCL_NVLS_ENABLE="0", KEBAB_SERPENTINE=serpentine)
         procs.append(subprocess.Popen([sys.executable, "-c", CHILD], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     outs = [p.communicate(timeout=300)[0] for p in procs]
     assert all(p.returncode == 0 for p in procs), "\n".join(o[-2000:] for o in outs)
-    assert "RESULT bitexact" in outs[0], outs[0][-2000:]
+    line = [ln for ln in outs[0].splitlines() if ln.startswith("RESULT")]
+    assert line, outs[0][-2000:]
+    return line[0]
+
+
+@pytest.mark.parametrize("version,pipeline", [(104, ""), (105, ""), (105, "1"), (107, "")])
+def test_sharded_bitexact(cuda, version, pipeline):
+    """With the serpentine K order off, a tile's summation order does not
+    depend on its place in the schedule: shards equal one GPU bit for bit."""
+    assert "RESULT bitexact" in _run(version, pipeline, "0")
+
+
+@pytest.mark.parametrize("version", [105, 107])
+def test_sharded_serpentine_within_tolerance(cuda, version):
+    """The default serpentine K order sums some tiles from the far end of K,
+    so shards may differ from one GPU in the last bits: within tolerance."""
+    line = _run(version, "", "1")
+    rel = float(line.split("rel_fro=")[1])
+    assert rel <= 1e-3, line

@@ -122,9 +122,10 @@ print(";".join(outs))
 
 
 @pytest.mark.gpu
-def test_serpentine_k_order_opt_in(cuda):
-    """KEBAB_SERPENTINE=1 (reverse K on alternate tiles of a CTA) stays
-    deterministic and within the FP16 tolerance of an FP32 reference."""
+def test_serpentine_k_order(cuda):
+    """The serpentine K order (the default; reverse K on alternate tiles of a
+    CTA) stays deterministic and within the FP16 tolerance of an FP32
+    reference."""
     env = dict(os.environ, KEBAB_SERPENTINE="1")
     r = subprocess.run([sys.executable, "-c", _SERP_SCRIPT, ROOT], env=env, capture_output=True, text=True,
                        timeout=600)
