@@ -537,12 +537,48 @@ class Extras:
             out["broadcast_gbs"] = 2.0 * S * S / (out["broadcast_ms"] * 1e-3) / 1e9
             out["broadcast_plus_gemm_ms"] = sorted(one(True) for _ in range(3))[1]
             out["broadcast_plus_gemm_tflops"] = 2.0 * S ** 3 / (out["broadcast_plus_gemm_ms"] * 1e-3) / 1e12
+            out["overlapped"] = self.chained(A, B, C, chunk_cols=1024, flops=2.0 * S ** 3)
         else:
             out["broadcast_ms"] = 0.0
             out["broadcast_plus_gemm_ms"] = out["ms_per_gemm"]
             out["broadcast_plus_gemm_tflops"] = out["tflops"]
         del data
         return out
+
+    def chained(self, A, B, C, chunk_cols, flops, reps=3):
+        """Broadcast of B overlapped with the GEMM: copy-engine pulls down the
+        rank chain (kebab_ring_pull) feeding each rank's gated GEMM
+        (kebab_gemm_gated). Device time from the GEMM's launch to its end,
+        max over ranks, median of `reps`; C is compared bit for bit with the
+        plain GEMM's (same rung, same schedule, same B)."""
+        torch = self.torch
+        from kebab_b200.shard import ChainBroadcastGemm
+        plain = C.clone()
+        chain = ChainBroadcastGemm(B, chunk_cols=chunk_cols)
+        times = []
+        try:
+            for r in range(reps + 1):  # the first call maps the peer buffer lazily: not timed
+                C.fill_(float("nan"))
+                self.sync()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+                chain.run(A, C, version=120, stream=self.stream)
+                e1.record(self.stream)
+                torch.cuda.synchronize()
+                rc, code = self.kb.device_status()
+                if rc != self.kb.OK:
+                    raise RuntimeError("device status 0x%x in the chained broadcast" % code)
+                if r:
+                    times.append(self.max_over_ranks(e0.elapsed_time(e1)))
+            same = self.all_true(torch.equal(C.view(torch.int16), plain.view(torch.int16)))
+        finally:
+            self.sync()
+            chain.close()
+        ms = sorted(times)[len(times) // 2]
+        return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "chunk_cols": chunk_cols, "chunks": chain.nchunks,
+                "bitexact_vs_plain_gemm": same,
+                "what": "B pulled down the rank chain by copy engines (CUDA IPC, NVLink) while every rank's gated "
+                        "GEMM runs; device time from GEMM launch to GEMM end, max over ranks, median of %d" % reps}
 
     def sparse(self, M, N, K, sets, steps, warmup):
         """A dense N(0,1) pruned 2:4 and compressed once
@@ -638,7 +674,8 @@ def main():
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=device)
+        import datetime
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
     dtype = torch.float16 if args.dtype == "fp16" else torch.bfloat16
     M, N, K = args.m, args.n, args.k
     M_global = M
@@ -798,7 +835,13 @@ def main():
         ser = sorted(one(False) for _ in range(3))[1]
         pip = sorted(one(True) for _ in range(3))[1]
         bcast_gemm = {"serial_ms": ser, "pipelined_ms": pip, "chunks": args.bcast_chunks,
-                      "what": "broadcast of B + this rank's GEMM, device time, max over ranks, median of 3"}
+                      "what": "broadcast of B + this rank's GEMM, device time, max over ranks, median of 3; "
+                              "pipelined = NCCL broadcast in N-chunks, one GEMM per chunk"}
+        try:
+            ex = Extras(torch, dist, kb, rank, world, device, stream, kb_sm_count(torch, local), cublas=False)
+            bcast_gemm["chained"] = ex.chained(As[0], Bs[0], Cs[0], chunk_cols=1024, flops=2.0 * M * N * K)
+        except Exception as e:  # reported, never silent
+            bcast_gemm["chained"] = {"error": str(e)[:300]}
 
     # End to end through the public API with host buffers: every step copies
     # its inputs host -> device from pinned memory (A shard; B on rank 0, then

@@ -51,7 +51,10 @@ KEBAB_DECLARE_RUNG(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowma
 #undef KEBAB_DECLARE_RUNG
 
 // The reference's own launcher names (kebab/include/kebab/cuda/cuda_gemm.h:43-257,
-// every non-template fp16 / bf16 launcher; the gemm_v2 template is left out),
+// every non-template fp16 / bf16 launcher except the v8..v12 names, whose
+// feature strings name the cluster load this build never issues; those ids
+// still reach their rung through baseline::gemm; the gemm_v2 template is
+// left out too),
 // each forwarding to the B200 rung its version id maps to (kebab_version_name()
 // tells which), with the same (A, B, C, M, N, K, lhs_format, rhs_format,
 // stream) arguments.
@@ -70,12 +73,6 @@ KEBAB_DECLARE_RUNG(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowma
   KEBAB_REFERENCE_ALIAS_F16(gemm_v5_wgmma_tma_warpgroup_warpspecialized_persistent_fp16, 5) \
   KEBAB_REFERENCE_ALIAS_F16(gemm_v6_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_fp16, 6) \
   KEBAB_REFERENCE_ALIAS_F16(gemm_v7_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_fp16, 7) \
-  KEBAB_REFERENCE_ALIAS_F16(gemm_v8_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_fp16, 8) \
-  KEBAB_REFERENCE_ALIAS_F16(gemm_v9_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_streamstore_fp16, 9) \
-  KEBAB_REFERENCE_ALIAS_F16(gemm_v10_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_fp16, 10) \
-  KEBAB_REFERENCE_ALIAS_F16(gemm_v11_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_fp16, 11) \
-  KEBAB_REFERENCE_ALIAS_BF16(gemm_v12_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_stmatrix_padded_bf16, 12) \
-  KEBAB_REFERENCE_ALIAS_F16(gemm_v12_wgmma_tma_warpgroup_warpspecialized_persistent_tilescheduler_ptxbarrier_tma5d_cluster_multicast_tmastore_hilbert_stmatrix_padded_fp16, 12) \
   KEBAB_REFERENCE_ALIAS_F16(gemm_v13_wgmma_tma_warpspecialized_persistent_tilescheduler_ptxbarrier_tma2d_fp16, 13) \
   KEBAB_REFERENCE_ALIAS_F16(gemm_v14_wgmma_tma_warpspecialized_persistent_ptxbarrier_tmastore_hilbert_stmatrix_padded_nocluster_fp16, 14) \
   KEBAB_REFERENCE_ALIAS_F16(gemm_v15_wgmma_tma_warpspecialized_ptxbarrier_tmastore_hilbert_stmatrix_padded_nocluster_nopersistent_fp16, 15) \

@@ -64,6 +64,20 @@ def lib():
         L.kebab_set_wait_timeout_us.restype = c.c_int
         L.kebab_probe_wait_timeout.argtypes = [c.c_void_p, c.c_uint64]
         L.kebab_probe_wait_timeout.restype = c.c_int
+        L.kebab_gemm_gated.argtypes = [c.c_int, c.c_void_p, c.c_void_p, c.c_void_p, c.c_int64, c.c_int64,
+                                       c.c_int64, c.c_int, c.c_void_p, c.c_int64, c.c_uint32, c.c_void_p]
+        L.kebab_gemm_gated.restype = c.c_int
+        L.kebab_ipc_export.argtypes = [c.c_void_p, c.c_void_p, c.POINTER(c.c_int64)]
+        L.kebab_ipc_export.restype = c.c_int
+        L.kebab_ipc_open.argtypes = [c.c_void_p, c.c_int64, c.POINTER(c.c_void_p)]
+        L.kebab_ipc_open.restype = c.c_int
+        L.kebab_ipc_close.argtypes = [c.c_void_p]
+        L.kebab_ipc_close.restype = c.c_int
+        L.kebab_flag_write.argtypes = [c.c_void_p, c.c_uint32, c.c_void_p]
+        L.kebab_flag_write.restype = c.c_int
+        L.kebab_ring_pull.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p, c.c_uint32,
+                                      c.c_void_p, c.c_void_p, c.c_void_p, c.c_uint64]
+        L.kebab_ring_pull.restype = c.c_int
         L.kebab_clock_probe.argtypes = [c.c_void_p, c.c_int64]
         L.kebab_clock_probe.restype = c.c_int
         L.kebab_shutdown.argtypes = []
@@ -142,6 +156,23 @@ def gemm(A, B, C=None, opmode="RC", version=HEURISTIC, stream=None):
     check(gemm_raw(_dtype_code(A), A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, opmode, version,
                    _stream_ptr(stream)))
     return C
+
+
+def gemm_gated(A, B, C, b_ready, chunk_cols, epoch, version=HEURISTIC, stream=None):
+    """kebab_gemm_gated: C = A * B (RC, shapes as gemm()) while B's columns
+    arrive in chunks of `chunk_cols`; a tile needing chunk j waits until the
+    int32 CUDA tensor b_ready[j] equals `epoch`."""
+    M, K = A.shape
+    N = B.shape[0]
+    check(lib().kebab_gemm_gated(_dtype_code(A), A.data_ptr(), B.data_ptr(), C.data_ptr(), M, N, K, version,
+                                 b_ready.data_ptr(), chunk_cols, epoch, _stream_ptr(stream)))
+    return C
+
+
+def flag_write(flag_ptr, value, stream=None):
+    """kebab_flag_write: a stream memory operation storing `value` at the
+    device address `flag_ptr` after the work already on `stream`."""
+    check(lib().kebab_flag_write(ctypes.c_void_p(flag_ptr), value, _stream_ptr(stream)))
 
 
 def device_status(stream=None, clear=True):

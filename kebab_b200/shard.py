@@ -9,6 +9,7 @@ has no multi-GPU path; this is the layout the north star asks for.
 The collectives go through torch.distributed, so the same host logic runs
 on `gloo` ranks on CPU (tests/test_shard.py) with a stand-in GEMM.
 """
+import os
 from dataclasses import dataclass
 
 TMA_ALIGN = 8  # rows of a shard: C's column pitch must stay 16-byte aligned
@@ -129,3 +130,128 @@ def gather_c(C_shard, world, group=None):
     staging = torch.empty((world * N, rows), dtype=C_shard.dtype, device=C_shard.device)
     dist.all_gather_into_tensor(staging, C_shard.contiguous(), group=group)
     return staging.view(world, N, rows).permute(1, 0, 2).reshape(N, world * rows)
+
+
+def chain_chunk_cols(N, K, elem_bytes=2, target_bytes=64 << 20, align=512):
+    """Columns per chunk of the chained broadcast: about `target_bytes` of B
+    per chunk, a multiple of `align` (the widest tile), at most N rounded up."""
+    cols = max(align, (target_bytes // (K * elem_bytes)) // align * align)
+    return min(cols, -(-N // align) * align)
+
+
+class ChainBroadcastGemm:
+    """Broadcast of B from rank 0 overlapped with every rank's GEMM on its
+    row block, with the copies on copy engines instead of SMs.
+
+    Rank r pulls B chunk by chunk from rank r-1 over NVLink (CUDA IPC mapping
+    of rank r-1's B, kebab_ring_pull) while its GEMM (kebab_gemm_gated, all
+    SMs) already runs and waits per tile, bounded, for the chunk the tile
+    needs. Which rank holds which chunk is shared through host shared memory
+    ([world, chunks] uint32 slots holding the call's epoch, a file in
+    /dev/shm created by rank 0 and unlinked once every rank has mapped it).
+
+    `B` is this rank's [N, K] buffer (rank 0's holds the data and is never
+    written; the others are overwritten by every call). Between calls that
+    rewrite B every rank must have returned (a barrier). Collective: every
+    rank constructs it and calls run() with the same shapes."""
+
+    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0):
+        import ctypes
+        import mmap
+        import uuid
+
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        import kebab_b200 as kb
+        self.kb, self.torch, self.dist, self.group = kb, torch, dist, group
+        self.B = B
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        N, K = B.shape
+        self.N, self.K = N, K
+        self.chunk_cols = chunk_cols or chain_chunk_cols(N, K, B.element_size())
+        self.chunk_bytes = self.chunk_cols * K * B.element_size()
+        self.total_bytes = N * K * B.element_size()
+        self.nchunks = -(-self.total_bytes // self.chunk_bytes)
+        self.timeout_us = int(timeout_s * 1e6)
+        self.ready = torch.zeros(self.nchunks, dtype=torch.int32, device=B.device)
+        self.epoch = 0
+        self.copy_stream = torch.cuda.Stream(device=B.device)
+        L = kb.lib()
+        # Every rank exports its B; rank r maps rank r-1's.
+        h = (ctypes.c_char * 64)()
+        off = ctypes.c_int64(0)
+        kb.check(L.kebab_ipc_export(ctypes.c_void_p(B.data_ptr()), h, ctypes.byref(off)))
+        handles = [None] * self.world
+        dist.all_gather_object(handles, (bytes(h), off.value), group=group)
+        self._src_handle = None
+        self.src_ptr = None
+        if self.rank > 0:
+            ph, poff = handles[self.rank - 1]
+            self._src_handle = ctypes.create_string_buffer(ph, 64)
+            p = ctypes.c_void_p(0)
+            kb.check(L.kebab_ipc_open(self._src_handle, poff, ctypes.byref(p)))
+            self.src_ptr = p.value
+        # Host slots shared by the ranks of the node.
+        nbytes = self.world * self.nchunks * 4
+        name = [None]
+        if self.rank == 0:
+            name[0] = "/dev/shm/kebab_chain_%d_%s" % (os.getpid(), uuid.uuid4().hex[:12])
+            with open(name[0], "wb") as f:
+                f.write(b"\0" * nbytes)
+        dist.broadcast_object_list(name, src=self._global(0), group=group)
+        fd = os.open(name[0], os.O_RDWR)
+        try:
+            self._mm = mmap.mmap(fd, nbytes)
+        finally:
+            os.close(fd)
+        self.slots = np.frombuffer(self._mm, dtype=np.uint32).reshape(self.world, self.nchunks)
+        self._anchor = ctypes.c_char.from_buffer(self._mm)
+        self._base = ctypes.addressof(self._anchor)
+        dist.barrier(group=group)
+        if self.rank == 0:
+            os.unlink(name[0])
+
+    def _global(self, r):
+        return r if self.group is None else self.dist.get_global_rank(self.group, r)
+
+    def _slot(self, r):
+        return self._base + r * self.nchunks * 4
+
+    def run(self, A, C, version=120, stream=None):
+        """C = A * B on this rank, B arriving from rank 0 during the GEMM.
+        Returns once this rank's copies have landed (its GEMM may still run
+        on `stream`)."""
+        import ctypes
+        torch, kb = self.torch, self.kb
+        stream = stream or torch.cuda.current_stream()
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        L = kb.lib()
+        if self.rank == 0:
+            kb.gemm(A, self.B, C, version=version, stream=stream)
+            kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), None, self.chunk_bytes, self.total_bytes,
+                                       None, self.epoch, None, ctypes.c_void_p(self._slot(0)), None,
+                                       self.timeout_us))
+            return C
+        # This call's copies overwrite B: after every earlier use of B on `stream`.
+        self.copy_stream.wait_stream(stream)
+        kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, self.epoch, version=version, stream=stream)
+        kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.src_ptr),
+                                   self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
+                                   self.epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
+                                   ctypes.c_void_p(self._slot(self.rank)),
+                                   ctypes.c_void_p(self.copy_stream.cuda_stream), self.timeout_us))
+        stream.wait_stream(self.copy_stream)
+        return C
+
+    def close(self):
+        if self._src_handle is not None:
+            self.kb.check(self.kb.lib().kebab_ipc_close(self._src_handle))
+            self._src_handle = None
+        self.slots = None
+        self._anchor = None
+        if getattr(self, "_mm", None) is not None:
+            self._mm.close()
+            self._mm = None

@@ -54,7 +54,7 @@ def test_reference_launcher_aliases_exported():
     out = subprocess.run(["nm", "-DC", kb.LIB_PATH], capture_output=True, text=True).stdout
     src = open(os.path.join(INC, "kebab", "cuda", "cuda_gemm.h")).read()
     aliases = re.findall(r"KEBAB_REFERENCE_ALIAS_(F16|BF16)\((gemm_\w+), (\d+)\)", src)
-    assert len(aliases) == 22
+    assert len(aliases) == 16
     for dt, name, vid in aliases:
         elem = "__half" if dt == "F16" else "__nv_bfloat16"
         assert "baseline::%s(%s const*" % (name, elem) in out, name

@@ -30,7 +30,17 @@ B = (torch.randn(N, K, generator=g, device=dev) / K ** 0.5).half()
 if rank != 0:
     B.zero_()
 blk = row_block(M, world, rank)
-if os.environ.get("KB_PIPELINE"):
+if os.environ.get("KB_CHAIN"):
+    from kebab_b200.shard import ChainBroadcastGemm
+    a = shard_a(A, blk).contiguous()
+    C = torch.empty((N, blk.rows), dtype=A.dtype, device=dev)
+    chain = ChainBroadcastGemm(B, chunk_cols=512)
+    for rep in range(2):  # the second call re-sends B over the same chain
+        chain.run(a, C, version=int(os.environ["KB_VERSION"]))
+        torch.cuda.synchronize()
+        dist.barrier()
+    chain.close()
+elif os.environ.get("KB_PIPELINE"):
     C = broadcast_gemm_pipelined(shard_a(A, blk).contiguous(), B, chunks=3, version=int(os.environ["KB_VERSION"]))
 else:
     broadcast_b(B, src=0)
@@ -57,7 +67,7 @@ def _port():
     return p
 
 
-def _run(version, pipeline, serpentine):
+def _run(version, pipeline, serpentine, chain=""):
     import torch
     world = min(torch.cuda.device_count(), 8)
     if world < 2:
@@ -67,7 +77,7 @@ def _run(version, pipeline, serpentine):
     for r in range(world):
         env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
                    MASTER_PORT=str(port), KB_ROOT=ROOT, KB_VERSION=str(version), KB_PIPELINE=pipeline,
-                   NCCL_NVLS_ENABLE="0", KEBAB_SERPENTINE=serpentine)
+                   NCCL_NVLS_ENABLE="0", KEBAB_SERPENTINE=serpentine, KB_CHAIN=chain)
         procs.append(subprocess.Popen([sys.executable, "-c", CHILD], env=env, stdout=subprocess.PIPE,
                                       stderr=subprocess.STDOUT, text=True))
     outs = [p.communicate(timeout=300)[0] for p in procs]
@@ -91,3 +101,10 @@ def test_sharded_serpentine_within_tolerance(cuda, version):
     line = _run(version, "", "1")
     rel = float(line.split("rel_fro=")[1])
     assert rel <= 1e-3, line
+
+
+@pytest.mark.parametrize("version", [105, 107])
+def test_chain_broadcast_gemm_bitexact(cuda, version):
+    """B pulled down the rank chain by copy engines while each rank's gated
+    GEMM runs: the gathered C equals one GPU's bit for bit."""
+    assert "RESULT bitexact" in _run(version, "", "0", chain="1")
