@@ -553,10 +553,29 @@ class Extras:
         plain GEMM's (same rung, same schedule, same B)."""
         torch = self.torch
         from kebab_b200.shard import ChainBroadcastGemm
-        plain = C.clone()
+        # The plain GEMM on the B every rank holds now, once after an idle
+        # barrier like the chained calls below (same power state).
+        plain = torch.empty_like(C)
+        singles = []
+        for _ in range(3):
+            self.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(self.stream)
+            self.kb.gemm(A, B, plain, version=120, stream=self.stream)
+            e1.record(self.stream)
+            torch.cuda.synchronize()
+            singles.append(self.max_over_ranks(e0.elapsed_time(e1)))
         chain = ChainBroadcastGemm(B, chunk_cols=chunk_cols)
-        times = []
+        times, copies, mine = [], [], []
         try:
+            for r in range(3):  # B alone down the chain: device time on the copy stream
+                self.sync()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(chain.copy_stream)
+                chain.run(None, None, stream=self.stream)
+                e1.record(chain.copy_stream)
+                torch.cuda.synchronize()
+                copies.append(self.max_over_ranks(e0.elapsed_time(e1)))
             for r in range(reps + 1):  # the first call maps the peer buffer lazily: not timed
                 C.fill_(float("nan"))
                 self.sync()
@@ -569,13 +588,21 @@ class Extras:
                 if rc != self.kb.OK:
                     raise RuntimeError("device status 0x%x in the chained broadcast" % code)
                 if r:
-                    times.append(self.max_over_ranks(e0.elapsed_time(e1)))
+                    mine.append(e0.elapsed_time(e1))
+                    times.append(self.max_over_ranks(mine[-1]))
             same = self.all_true(torch.equal(C.view(torch.int16), plain.view(torch.int16)))
         finally:
             self.sync()
             chain.close()
         ms = sorted(times)[len(times) // 2]
-        return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "chunk_cols": chunk_cols, "chunks": chain.nchunks,
+        per_rank = [None] * self.world
+        if self.world > 1:
+            self.dist.all_gather_object(per_rank, sorted(mine)[len(mine) // 2])
+        copy_ms = sorted(copies)[1]
+        return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "per_rank_ms": per_rank,
+                "gemm_single_ms": sorted(singles)[1], "copy_only_ms": copy_ms,
+                "copy_only_gbs": B.numel() * B.element_size() / (copy_ms * 1e-3) / 1e9,
+                "chunk_cols": chunk_cols, "chunks": chain.nchunks,
                 "bitexact_vs_plain_gemm": same,
                 "what": "B pulled down the rank chain by copy engines (CUDA IPC, NVLink) while every rank's gated "
                         "GEMM runs; device time from GEMM launch to GEMM end, max over ranks, median of %d" % reps}

@@ -86,7 +86,7 @@ __device__ __forceinline__ void st_async_v4(uint32_t dst, uint32_t bar, const ui
 template <typename T, int BNM, int KSUB, int STAGES, int SPLITS>
 __global__ void __launch_bounds__(192, 1)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmA, T* C, int M,
-                       int N, int K, int pdl, WaitCtx ctx) {
+                       int N, int K, int step, int pdl, WaitCtx ctx) {
   using L = SkinnySmem<BNM, KSUB, STAGES>;
   constexpr uint32_t IDESC = umma_idesc_f16(BMM, BNM, ElemTraits<T>::kBf16);
   constexpr uint32_t TMEM_COLS = BNM;
@@ -101,7 +101,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ks = (int)cluster_ctarank();
-  const int n0 = (blockIdx.x / SPLITS) * BMM;
+  // Tiles start every `step` (<= BMM) columns n of C: with step < BMM the
+  // 128-row MMA tiles overlap, so that tiles x splits can fill the SMs; each
+  // CTA stores only its own `step` rows.
+  const int n0 = (blockIdx.x / SPLITS) * step;
   const int m0 = blockIdx.y * BNM;  // M-tile (M > BNM)
   const int kb_total = (K + BK * KSUB - 1) / (BK * KSUB);
   const int kb_per = (kb_total + SPLITS - 1) / SPLITS;
@@ -256,7 +259,7 @@ __global__ void __launch_bounds__(192, 1)
     const int c0 = m0 + ks * CS;
     const int n = n0 + row;
     T* out = C + (size_t)n * M;
-    if (got && n < N) {
+    if (got && n < N && row < step) {
 #pragma unroll
       for (int cc = 0; cc < CS; cc += 8) {
         float acc[8];
@@ -305,8 +308,7 @@ __global__ void __launch_bounds__(192, 1)
 
 template <typename T, int BNM, int KSUB, int STAGES, int SPLITS>
 int launch_splits(const GemmProblem& p, const CUtensorMap& tBt, const CUtensorMap& tA, int64_t tiles_n,
-                  int64_t tiles_m,
-                  const WaitCtx& ctx) {
+                  int64_t tiles_m, int step, const WaitCtx& ctx) {
   using L = SkinnySmem<BNM, KSUB, STAGES>;
   auto kern = gemm_skinny_kernel<T, BNM, KSUB, STAGES, SPLITS>;
   // Shared-memory opt-in once per device (host cost, not per launch).
@@ -333,7 +335,7 @@ int launch_splits(const GemmProblem& p, const CUtensorMap& tBt, const CUtensorMa
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  e = cudaLaunchKernelEx(&cfg, kern, tBt, tA, static_cast<T*>(p.C), (int)p.M, (int)p.N, (int)p.K,
+  e = cudaLaunchKernelEx(&cfg, kern, tBt, tA, static_cast<T*>(p.C), (int)p.M, (int)p.N, (int)p.K, step,
                          cfg.numAttrs == 2 ? 1 : 0, ctx);
   if (e != cudaSuccess) return cuda_fail(e, "gemm_v106 launch");
   return KEBAB_OK;
@@ -353,23 +355,43 @@ int launch(const GemmProblem& p, int splits_override) {
   CUtensorMap tBt, tA;
   if ((rc = make_tmap_2d(&tBt, p.B, p.dtype, p.N, p.K, p.K, BMM, BK, true))) return rc;
   if ((rc = make_tmap_2d(&tA, p.A, p.dtype, p.M, p.K, p.K, BNM, BK, true))) return rc;
-  const int64_t tiles_n = (p.N + BMM - 1) / BMM, tiles_m = (p.M + BNM - 1) / BNM;
+  int64_t tiles_n = (p.N + BMM - 1) / BMM;
+  const int64_t tiles_m = (p.M + BNM - 1) / BNM;
   const int64_t tiles = tiles_n * tiles_m;
   const int kb_total = (int)((p.K + BK * KSUB - 1) / (BK * KSUB));
+  const long long slots = (long long)L::PER_SM * dev->sm_count;
   int splits = splits_override;
   if (splits <= 0) {
     // As many CTAs as fit in one wave (L::PER_SM per SM), in powers of two up
     // to the portable cluster size.
     splits = 1;
-    while (splits < 8 && tiles * splits * 2 <= (long long)L::PER_SM * dev->sm_count && splits * 2 <= kb_total)
-      splits *= 2;
+    while (splits < 8 && tiles * splits * 2 <= slots && splits * 2 <= kb_total) splits *= 2;
+  }
+  // Fit the wave: when tiles x splits leaves SMs idle (64 x 8192 x 8192: 64
+  // tiles x 2 = 128 CTAs on 148 SMs), start tiles every `step` < 128 columns
+  // (a multiple of 8) so that more of them fill the wave. Neighbouring tiles
+  // then read a few B^T rows twice, from L2, as they run side by side.
+  int step = BMM;
+  static const bool fit_env = [] {
+    const char* e = std::getenv("KEBAB_V106_FIT");
+    return !(e && e[0] == '0');
+  }();
+  if (fit_env && tiles * splits < slots) {
+    const long long want = slots / ((long long)splits * tiles_m);
+    if (want > tiles_n) {
+      const int64_t st = (((p.N + want - 1) / want) + 7) / 8 * 8;
+      if (st < BMM) {
+        step = (int)st;
+        tiles_n = (p.N + st - 1) / st;
+      }
+    }
   }
   if (tiles_n * splits > INT32_MAX || tiles_m > 65535) return fail(KEBAB_EINVAL, "grid too large for v106");
   switch (splits) {
-    case 1: return launch_splits<T, BNM, KSUB, STAGES, 1>(p, tBt, tA, tiles_n, tiles_m, ctx);
-    case 2: return launch_splits<T, BNM, KSUB, STAGES, 2>(p, tBt, tA, tiles_n, tiles_m, ctx);
-    case 4: return launch_splits<T, BNM, KSUB, STAGES, 4>(p, tBt, tA, tiles_n, tiles_m, ctx);
-    case 8: return launch_splits<T, BNM, KSUB, STAGES, 8>(p, tBt, tA, tiles_n, tiles_m, ctx);
+    case 1: return launch_splits<T, BNM, KSUB, STAGES, 1>(p, tBt, tA, tiles_n, tiles_m, step, ctx);
+    case 2: return launch_splits<T, BNM, KSUB, STAGES, 2>(p, tBt, tA, tiles_n, tiles_m, step, ctx);
+    case 4: return launch_splits<T, BNM, KSUB, STAGES, 4>(p, tBt, tA, tiles_n, tiles_m, step, ctx);
+    case 8: return launch_splits<T, BNM, KSUB, STAGES, 8>(p, tBt, tA, tiles_n, tiles_m, step, ctx);
     default: return fail(KEBAB_EINVAL, "splits must be 1, 2, 4 or 8");
   }
 }

@@ -223,21 +223,23 @@ class ChainBroadcastGemm:
     def run(self, A, C, version=120, stream=None):
         """C = A * B on this rank, B arriving from rank 0 during the GEMM.
         Returns once this rank's copies have landed (its GEMM may still run
-        on `stream`)."""
+        on `stream`). With A None only B is broadcast (no GEMM)."""
         import ctypes
         torch, kb = self.torch, self.kb
         stream = stream or torch.cuda.current_stream()
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
         L = kb.lib()
         if self.rank == 0:
-            kb.gemm(A, self.B, C, version=version, stream=stream)
+            if A is not None:
+                kb.gemm(A, self.B, C, version=version, stream=stream)
             kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), None, self.chunk_bytes, self.total_bytes,
                                        None, self.epoch, None, ctypes.c_void_p(self._slot(0)), None,
                                        self.timeout_us))
             return C
         # This call's copies overwrite B: after every earlier use of B on `stream`.
         self.copy_stream.wait_stream(stream)
-        kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, self.epoch, version=version, stream=stream)
+        if A is not None:
+            kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, self.epoch, version=version, stream=stream)
         kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.src_ptr),
                                    self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
                                    self.epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
