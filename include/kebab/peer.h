@@ -68,11 +68,14 @@ int kebab_gemm_gated(kebab_dtype dtype, const void* A, const void* B, void* C, i
  * waits until have_src[j] == epoch, then on `stream` copies the chunk from
  * src to dst (copy engine, peer memory), raises the device flag ready[j] to
  * epoch (stream memory operation) and records an event; as the events
- * complete, sets have_mine[j] = epoch. Returns once every chunk has landed,
- * or KEBAB_ETIMEOUT when no progress is made for `timeout_us`. */
+ * complete, sets have_mine[j] = epoch. With a non-NULL `stream2` each chunk
+ * is copied as two halves, the second on stream2 (two copy engines), and the
+ * flag waits for both; stream2 must already be ordered after earlier users of
+ * dst, like `stream`. Returns once every chunk has landed, or KEBAB_ETIMEOUT
+ * when no progress is made for `timeout_us`. */
 int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t total_bytes, uint32_t* ready,
                     uint32_t epoch, const uint32_t* have_src, uint32_t* have_mine, kebab_stream_t stream,
-                    uint64_t timeout_us);
+                    kebab_stream_t stream2, uint64_t timeout_us);
 
 #ifdef __cplusplus
 }

@@ -135,7 +135,7 @@ int kebab_flag_write(uint32_t* flag, uint32_t value, kebab_stream_t stream) {
 
 int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t total_bytes, uint32_t* ready,
                     uint32_t epoch, const uint32_t* have_src, uint32_t* have_mine, kebab_stream_t stream,
-                    uint64_t timeout_us) {
+                    kebab_stream_t stream2, uint64_t timeout_us) {
   if (!dst || !have_mine || chunk_bytes <= 0 || total_bytes <= 0 || (src && (!have_src || !ready)))
     return fail(KEBAB_EINVAL, "bad arguments to kebab_ring_pull");
   if (epoch == 0) return fail(KEBAB_EINVAL, "kebab_ring_pull: epoch 0 is the value of never-written slots");
@@ -150,7 +150,8 @@ int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t tot
   }
   const auto* prev = reinterpret_cast<const std::atomic<uint32_t>*>(have_src);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  while ((int64_t)t_events.size() < nchunks) {
+  cudaStream_t s2 = reinterpret_cast<cudaStream_t>(stream2);
+  while ((int64_t)t_events.size() < 2 * nchunks) {
     cudaEvent_t ev;
     cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
     if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
@@ -174,9 +175,20 @@ int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t tot
     if (issued < nchunks && prev[issued].load(std::memory_order_acquire) == epoch) {
       const int64_t off = issued * chunk_bytes;
       const int64_t n = std::min(chunk_bytes, total_bytes - off);
-      cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dst) + off, static_cast<const uint8_t*>(src) + off,
-                                      (size_t)n, cudaMemcpyDeviceToDevice, s);
+      // With a second stream the chunk is split in two copies that can run
+      // on two copy engines; the flag waits for both.
+      const int64_t n1 = s2 ? std::min(n, ((n / 2) + 255) / 256 * 256) : n;
+      uint8_t* d = static_cast<uint8_t*>(dst) + off;
+      const uint8_t* sp = static_cast<const uint8_t*>(src) + off;
+      cudaError_t e = cudaMemcpyAsync(d, sp, (size_t)n1, cudaMemcpyDeviceToDevice, s);
       if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(chunk from the previous rank)");
+      if (s2 && n > n1) {
+        cudaEvent_t half = t_events[nchunks + issued];
+        if ((e = cudaMemcpyAsync(d + n1, sp + n1, (size_t)(n - n1), cudaMemcpyDeviceToDevice, s2)) != cudaSuccess)
+          return cuda_fail(e, "cudaMemcpyAsync(second half of a chunk)");
+        if ((e = cudaEventRecord(half, s2)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+        if ((e = cudaStreamWaitEvent(s, half, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+      }
       CUresult r = g_write_value(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(ready + issued), epoch, 0);
       if (r != CUDA_SUCCESS) return fail(KEBAB_ECUDA, "cuStreamWriteValue32 failed with CUresult " + std::to_string(r));
       if ((e = cudaEventRecord(t_events[issued], s)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");

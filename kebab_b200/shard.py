@@ -155,7 +155,7 @@ class ChainBroadcastGemm:
     rewrite B every rank must have returned (a barrier). Collective: every
     rank constructs it and calls run() with the same shapes."""
 
-    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0):
+    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=2):
         import ctypes
         import mmap
         import uuid
@@ -179,6 +179,7 @@ class ChainBroadcastGemm:
         self.ready = torch.zeros(self.nchunks, dtype=torch.int32, device=B.device)
         self.epoch = 0
         self.copy_stream = torch.cuda.Stream(device=B.device)
+        self.copy_stream2 = torch.cuda.Stream(device=B.device) if copy_streams > 1 else None
         L = kb.lib()
         # Every rank exports its B; rank r maps rank r-1's.
         h = (ctypes.c_char * 64)()
@@ -233,18 +234,22 @@ class ChainBroadcastGemm:
             if A is not None:
                 kb.gemm(A, self.B, C, version=version, stream=stream)
             kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), None, self.chunk_bytes, self.total_bytes,
-                                       None, self.epoch, None, ctypes.c_void_p(self._slot(0)), None,
+                                       None, self.epoch, None, ctypes.c_void_p(self._slot(0)), None, None,
                                        self.timeout_us))
             return C
         # This call's copies overwrite B: after every earlier use of B on `stream`.
         self.copy_stream.wait_stream(stream)
+        if self.copy_stream2 is not None:
+            self.copy_stream2.wait_stream(stream)
         if A is not None:
             kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, self.epoch, version=version, stream=stream)
         kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.src_ptr),
                                    self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
                                    self.epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
                                    ctypes.c_void_p(self._slot(self.rank)),
-                                   ctypes.c_void_p(self.copy_stream.cuda_stream), self.timeout_us))
+                                   ctypes.c_void_p(self.copy_stream.cuda_stream),
+                                   ctypes.c_void_p(self.copy_stream2.cuda_stream if self.copy_stream2 else None),
+                                   self.timeout_us))
         stream.wait_stream(self.copy_stream)
         return C
 

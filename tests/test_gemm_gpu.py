@@ -75,9 +75,11 @@ def test_timeout_probe(cuda):
 
 # ----------------------------------------------------------------------------- skinny (v106)
 @pytest.mark.parametrize("M", [8, 64, 72, 128, 200, 256])
-@pytest.mark.parametrize("splits", ["", "1", "2", "8"])
-def test_skinny_v106(cuda, M, splits, monkeypatch):
+@pytest.mark.parametrize("splits,fit", [("", ""), ("1", ""), ("2", ""), ("8", ""), ("", "1"), ("2", "1")])
+def test_skinny_v106(cuda, M, splits, fit, monkeypatch):
+    """fit=1: overlapping 128-row tiles started every < 128 columns."""
     monkeypatch.setenv("KEBAB_V106_SPLITS", splits)
+    monkeypatch.setenv("KEBAB_V106_FIT", fit)
     N, K = 1000, 1536
     A, B = inputs(M, N, K, seed=M, dtype=O.F16)
     assert_close(run(A, B, M, N, K, O.F16, 106, cuda), O.gemm(A, B, M, N, K, O.F16), "v106 M=%d s=%s" % (M, splits))
