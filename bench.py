@@ -538,7 +538,8 @@ class Extras:
             out["broadcast_plus_gemm_ms"] = sorted(one(True) for _ in range(3))[1]
             out["broadcast_plus_gemm_tflops"] = 2.0 * S ** 3 / (out["broadcast_plus_gemm_ms"] * 1e-3) / 1e12
             cols = int(os.environ.get("KEBAB_BENCH_CHAIN_COLS", "0")) or (1024 if self.world <= 2 else 512)
-            out["overlapped"] = self.chained(A, B, C, chunk_cols=cols, flops=2.0 * S ** 3)
+            out["overlapped"] = self.chained(A, B, C, chunk_cols=cols, flops=2.0 * S ** 3, mode="push")
+            out["overlapped_pull"] = self.chained(A, B, C, chunk_cols=cols, flops=2.0 * S ** 3, mode="pull")
         else:
             out["broadcast_ms"] = 0.0
             out["broadcast_plus_gemm_ms"] = out["ms_per_gemm"]
@@ -546,7 +547,7 @@ class Extras:
         del data
         return out
 
-    def chained(self, A, B, C, chunk_cols, flops, reps=3):
+    def chained(self, A, B, C, chunk_cols, flops, reps=3, mode="push"):
         """Broadcast of B overlapped with the GEMM: copy-engine pulls down the
         rank chain (kebab_ring_pull) feeding each rank's gated GEMM
         (kebab_gemm_gated). Device time from the GEMM's launch to its end,
@@ -566,17 +567,18 @@ class Extras:
             e1.record(self.stream)
             torch.cuda.synchronize()
             singles.append(self.max_over_ranks(e0.elapsed_time(e1)))
-        chain = ChainBroadcastGemm(B, chunk_cols=chunk_cols)
-        times, copies, mine = [], [], []
+        chain = ChainBroadcastGemm(B, chunk_cols=chunk_cols, mode=mode)
+        times, copies, mine, mine_copy = [], [], [], []
         try:
             for r in range(3):  # B alone down the chain: device time on the copy stream
                 self.sync()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(chain.copy_stream)
+                e0.record(self.stream)
                 chain.run(None, None, stream=self.stream)
-                e1.record(chain.copy_stream)
+                e1.record(self.stream)
                 torch.cuda.synchronize()
-                copies.append(self.max_over_ranks(e0.elapsed_time(e1)))
+                mine_copy.append(e0.elapsed_time(e1))
+                copies.append(self.max_over_ranks(mine_copy[-1]))
             for r in range(reps + 1):  # the first call maps the peer buffer lazily: not timed
                 C.fill_(float("nan"))
                 self.sync()
@@ -597,16 +599,20 @@ class Extras:
             chain.close()
         ms = sorted(times)[len(times) // 2]
         per_rank = [None] * self.world
+        per_rank_copy = [None] * self.world
         if self.world > 1:
             self.dist.all_gather_object(per_rank, sorted(mine)[len(mine) // 2])
+            self.dist.all_gather_object(per_rank_copy, sorted(mine_copy)[1])
         copy_ms = sorted(copies)[1]
-        return {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "per_rank_ms": per_rank,
+        return {"mode": mode, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "per_rank_ms": per_rank,
+                "per_rank_copy_ms": per_rank_copy,
                 "gemm_single_ms": sorted(singles)[1], "copy_only_ms": copy_ms,
                 "copy_only_gbs": B.numel() * B.element_size() / (copy_ms * 1e-3) / 1e9,
                 "chunk_cols": chunk_cols, "chunks": chain.nchunks,
                 "bitexact_vs_plain_gemm": same,
-                "what": "B pulled down the rank chain by copy engines (CUDA IPC, NVLink) while every rank's gated "
-                        "GEMM runs; device time from GEMM launch to GEMM end, max over ranks, median of %d" % reps}
+                "what": "B moved down the rank chain by copy engines (CUDA IPC, NVLink; %s) while every rank's gated "
+                        "GEMM runs; device time from GEMM launch to GEMM end, max over ranks, median of %d; "
+                        "copy_only: the same chain without GEMMs" % (mode, reps)}
 
     def sparse(self, M, N, K, sets, steps, warmup):
         """A dense N(0,1) pruned 2:4 and compressed once

@@ -77,6 +77,22 @@ int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t tot
                     uint32_t epoch, const uint32_t* have_src, uint32_t* have_mine, kebab_stream_t stream,
                     kebab_stream_t stream2, uint64_t timeout_us);
 
+/* One link of the broadcast chain, push direction: this rank writes each
+ * chunk into the next rank's buffer. `have_mine` / `have_next` are the
+ * host-shared slots of this rank and of the next one.
+ * For each chunk j: waits until this rank holds it (have_mine[j] == epoch;
+ * have_mine NULL = the source rank, which holds every chunk), then on
+ * `stream` copies it from src to dst_next (copy engine, peer memory; split
+ * over stream2 as in kebab_ring_pull), writes the next rank's device flag
+ * ready_next[j] = epoch (a stream memory operation on peer memory, ordered
+ * after the copy) and, once the copy has completed, sets have_next[j] =
+ * epoch. The last rank passes dst_next = NULL and only waits until every
+ * have_mine[j] == epoch. Returns once done, or KEBAB_ETIMEOUT when no
+ * progress is made for `timeout_us`. */
+int kebab_chain_push(const void* src, void* dst_next, int64_t chunk_bytes, int64_t total_bytes, uint32_t* ready_next,
+                     uint32_t epoch, const uint32_t* have_mine, uint32_t* have_next, kebab_stream_t stream,
+                     kebab_stream_t stream2, uint64_t timeout_us);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,9 @@ def lib():
         L.kebab_ring_pull.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p, c.c_uint32,
                                       c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_uint64]
         L.kebab_ring_pull.restype = c.c_int
+        L.kebab_chain_push.argtypes = [c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_void_p, c.c_uint32,
+                                       c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p, c.c_uint64]
+        L.kebab_chain_push.restype = c.c_int
         L.kebab_clock_probe.argtypes = [c.c_void_p, c.c_int64]
         L.kebab_clock_probe.restype = c.c_int
         L.kebab_shutdown.argtypes = []

@@ -211,4 +211,82 @@ int kebab_ring_pull(void* dst, const void* src, int64_t chunk_bytes, int64_t tot
   return KEBAB_OK;
 }
 
+int kebab_chain_push(const void* src, void* dst_next, int64_t chunk_bytes, int64_t total_bytes, uint32_t* ready_next,
+                     uint32_t epoch, const uint32_t* have_mine, uint32_t* have_next, kebab_stream_t stream,
+                     kebab_stream_t stream2, uint64_t timeout_us) {
+  if (!src || chunk_bytes <= 0 || total_bytes <= 0 || (dst_next && (!ready_next || !have_next)) ||
+      (!dst_next && !have_mine))
+    return fail(KEBAB_EINVAL, "bad arguments to kebab_chain_push");
+  if (epoch == 0) return fail(KEBAB_EINVAL, "kebab_chain_push: epoch 0 is the value of never-written slots");
+  int rc = peer_fns();
+  if (rc) return rc;
+  const int64_t nchunks = (total_bytes + chunk_bytes - 1) / chunk_bytes;
+  const auto* mine = reinterpret_cast<const std::atomic<uint32_t>*>(have_mine);
+  auto* next = reinterpret_cast<std::atomic<uint32_t>*>(have_next);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  cudaStream_t s2 = reinterpret_cast<cudaStream_t>(stream2);
+  while ((int64_t)t_events.size() < 2 * nchunks) {
+    cudaEvent_t ev;
+    cudaError_t e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    t_events.push_back(ev);
+  }
+  auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(timeout_us);
+  int64_t issued = 0, published = 0;
+  const int64_t goal = dst_next ? nchunks : 0;  // the last rank forwards nothing
+  int64_t arrived = 0;                          // last rank: chunks seen landed
+  while (published < goal || (!dst_next && arrived < nchunks)) {
+    bool progressed = false;
+    if (!dst_next) {
+      while (arrived < nchunks && mine[arrived].load(std::memory_order_acquire) == epoch) {
+        ++arrived;
+        progressed = true;
+      }
+    } else {
+      if (issued < nchunks && (!have_mine || mine[issued].load(std::memory_order_acquire) == epoch)) {
+        const int64_t off = issued * chunk_bytes;
+        const int64_t n = std::min(chunk_bytes, total_bytes - off);
+        const int64_t n1 = s2 ? std::min(n, ((n / 2) + 255) / 256 * 256) : n;
+        uint8_t* d = static_cast<uint8_t*>(dst_next) + off;
+        const uint8_t* sp = static_cast<const uint8_t*>(src) + off;
+        cudaError_t e = cudaMemcpyAsync(d, sp, (size_t)n1, cudaMemcpyDeviceToDevice, s);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(chunk to the next rank)");
+        if (s2 && n > n1) {
+          cudaEvent_t half = t_events[nchunks + issued];
+          if ((e = cudaMemcpyAsync(d + n1, sp + n1, (size_t)(n - n1), cudaMemcpyDeviceToDevice, s2)) != cudaSuccess)
+            return cuda_fail(e, "cudaMemcpyAsync(second half of a chunk)");
+          if ((e = cudaEventRecord(half, s2)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+          if ((e = cudaStreamWaitEvent(s, half, 0)) != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+        }
+        // The next rank's device flag, written over NVLink after the chunk.
+        CUresult r = g_write_value(reinterpret_cast<CUstream>(s), reinterpret_cast<CUdeviceptr>(ready_next + issued),
+                                   epoch, 0);
+        if (r != CUDA_SUCCESS)
+          return fail(KEBAB_ECUDA, "cuStreamWriteValue32 (peer flag) failed with CUresult " + std::to_string(r));
+        if ((e = cudaEventRecord(t_events[issued], s)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+        ++issued;
+        progressed = true;
+      }
+      while (published < issued) {
+        cudaError_t e = cudaEventQuery(t_events[published]);
+        if (e == cudaErrorNotReady) break;
+        if (e != cudaSuccess) return cuda_fail(e, "cudaEventQuery(chunk copy)");
+        next[published].store(epoch, std::memory_order_release);
+        ++published;
+        progressed = true;
+      }
+    }
+    if (progressed) {
+      deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(timeout_us);
+    } else {
+      if (std::chrono::steady_clock::now() > deadline)
+        return fail(KEBAB_ETIMEOUT, "kebab_chain_push: timed out with " + std::to_string(issued) + " of " +
+                                        std::to_string(nchunks) + " chunks pushed, " + std::to_string(published) +
+                                        " landed, " + std::to_string(arrived) + " received");
+      std::this_thread::yield();
+    }
+  }
+  return KEBAB_OK;
+}
+
 }  // extern "C"

@@ -143,19 +143,23 @@ class ChainBroadcastGemm:
     """Broadcast of B from rank 0 overlapped with every rank's GEMM on its
     row block, with the copies on copy engines instead of SMs.
 
-    Rank r pulls B chunk by chunk from rank r-1 over NVLink (CUDA IPC mapping
-    of rank r-1's B, kebab_ring_pull) while its GEMM (kebab_gemm_gated, all
-    SMs) already runs and waits per tile, bounded, for the chunk the tile
-    needs. Which rank holds which chunk is shared through host shared memory
-    ([world, chunks] uint32 slots holding the call's epoch, a file in
-    /dev/shm created by rank 0 and unlinked once every rank has mapped it).
+    B moves down the rank chain 0 -> 1 -> ... -> P-1 in chunks over NVLink
+    (CUDA IPC mappings of the neighbours' buffers), each chunk forwarded as
+    soon as it has landed, while every rank's GEMM (kebab_gemm_gated on ranks
+    >= 1, all SMs) already runs and waits per tile, bounded, for the chunk the
+    tile needs. mode "push": rank r writes chunk j into rank r+1's B and then
+    raises rank r+1's device flag over NVLink (kebab_chain_push); mode "pull":
+    rank r copies chunk j out of rank r-1's B and raises its own flag
+    (kebab_ring_pull). Which rank holds which chunk is shared through host
+    shared memory ([P, chunks] uint32 slots holding the call's epoch, plus
+    one "ready to receive" slot per rank; a file in /dev/shm created by rank
+    0 and unlinked once every rank has mapped it).
 
     `B` is this rank's [N, K] buffer (rank 0's holds the data and is never
-    written; the others are overwritten by every call). Between calls that
-    rewrite B every rank must have returned (a barrier). Collective: every
+    written; the others are overwritten by every call). Collective: every
     rank constructs it and calls run() with the same shapes."""
 
-    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=2):
+    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=2, mode="push"):
         import ctypes
         import mmap
         import uuid
@@ -165,7 +169,10 @@ class ChainBroadcastGemm:
         import torch.distributed as dist
 
         import kebab_b200 as kb
+        if mode not in ("push", "pull"):
+            raise ShardError("mode must be push or pull")
         self.kb, self.torch, self.dist, self.group = kb, torch, dist, group
+        self.mode = mode
         self.B = B
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -175,28 +182,40 @@ class ChainBroadcastGemm:
         self.chunk_bytes = self.chunk_cols * K * B.element_size()
         self.total_bytes = N * K * B.element_size()
         self.nchunks = -(-self.total_bytes // self.chunk_bytes)
+        self.timeout_s = timeout_s
         self.timeout_us = int(timeout_s * 1e6)
         self.ready = torch.zeros(self.nchunks, dtype=torch.int32, device=B.device)
         self.epoch = 0
         self.copy_stream = torch.cuda.Stream(device=B.device)
         self.copy_stream2 = torch.cuda.Stream(device=B.device) if copy_streams > 1 else None
         L = kb.lib()
-        # Every rank exports its B; rank r maps rank r-1's.
-        h = (ctypes.c_char * 64)()
-        off = ctypes.c_int64(0)
-        kb.check(L.kebab_ipc_export(ctypes.c_void_p(B.data_ptr()), h, ctypes.byref(off)))
+
+        def export(t):
+            h = (ctypes.c_char * 64)()
+            off = ctypes.c_int64(0)
+            kb.check(L.kebab_ipc_export(ctypes.c_void_p(t.data_ptr()), h, ctypes.byref(off)))
+            return bytes(h), off.value
+
         handles = [None] * self.world
-        dist.all_gather_object(handles, (bytes(h), off.value), group=group)
-        self._src_handle = None
-        self.src_ptr = None
-        if self.rank > 0:
-            ph, poff = handles[self.rank - 1]
-            self._src_handle = ctypes.create_string_buffer(ph, 64)
+        dist.all_gather_object(handles, (export(B), export(self.ready)), group=group)
+        self._opened = []
+
+        def open_(hoff):
+            hb = ctypes.create_string_buffer(hoff[0], 64)
             p = ctypes.c_void_p(0)
-            kb.check(L.kebab_ipc_open(self._src_handle, poff, ctypes.byref(p)))
-            self.src_ptr = p.value
-        # Host slots shared by the ranks of the node.
-        nbytes = self.world * self.nchunks * 4
+            kb.check(L.kebab_ipc_open(hb, hoff[1], ctypes.byref(p)))
+            self._opened.append(hb)
+            return p.value
+
+        self.src_ptr = self.next_b = self.next_ready = None
+        if mode == "pull" and self.rank > 0:
+            self.src_ptr = open_(handles[self.rank - 1][0])
+        if mode == "push" and self.rank + 1 < self.world:
+            self.next_b = open_(handles[self.rank + 1][0])
+            self.next_ready = open_(handles[self.rank + 1][1])
+        # Host slots shared by the ranks of the node: [P, chunks] chunk slots,
+        # then P "ready to receive" slots.
+        nbytes = (self.world * self.nchunks + self.world) * 4
         name = [None]
         if self.rank == 0:
             name[0] = "/dev/shm/kebab_chain_%d_%s" % (os.getpid(), uuid.uuid4().hex[:12])
@@ -208,7 +227,9 @@ class ChainBroadcastGemm:
             self._mm = mmap.mmap(fd, nbytes)
         finally:
             os.close(fd)
-        self.slots = np.frombuffer(self._mm, dtype=np.uint32).reshape(self.world, self.nchunks)
+        flat = np.frombuffer(self._mm, dtype=np.uint32)
+        self.slots = flat[:self.world * self.nchunks].reshape(self.world, self.nchunks)
+        self.recv_ok = flat[self.world * self.nchunks:]
         self._anchor = ctypes.c_char.from_buffer(self._mm)
         self._base = ctypes.addressof(self._anchor)
         dist.barrier(group=group)
@@ -223,41 +244,66 @@ class ChainBroadcastGemm:
 
     def run(self, A, C, version=120, stream=None):
         """C = A * B on this rank, B arriving from rank 0 during the GEMM.
-        Returns once this rank's copies have landed (its GEMM may still run
-        on `stream`). With A None only B is broadcast (no GEMM)."""
+        Returns once this rank's part of the broadcast is done (its chunks
+        landed and, in push mode, forwarded); its GEMM may still run on
+        `stream`. With A None only B is broadcast (no GEMM)."""
         import ctypes
+        import time
         torch, kb = self.torch, self.kb
         stream = stream or torch.cuda.current_stream()
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        epoch = self.epoch
         L = kb.lib()
-        if self.rank == 0:
-            if A is not None:
-                kb.gemm(A, self.B, C, version=version, stream=stream)
-            kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), None, self.chunk_bytes, self.total_bytes,
-                                       None, self.epoch, None, ctypes.c_void_p(self._slot(0)), None, None,
-                                       self.timeout_us))
-            return C
+        s1 = ctypes.c_void_p(self.copy_stream.cuda_stream)
+        s2 = ctypes.c_void_p(self.copy_stream2.cuda_stream if self.copy_stream2 else None)
         # This call's copies overwrite B: after every earlier use of B on `stream`.
         self.copy_stream.wait_stream(stream)
         if self.copy_stream2 is not None:
             self.copy_stream2.wait_stream(stream)
-        if A is not None:
-            kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, self.epoch, version=version, stream=stream)
-        kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.src_ptr),
-                                   self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
-                                   self.epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
-                                   ctypes.c_void_p(self._slot(self.rank)),
-                                   ctypes.c_void_p(self.copy_stream.cuda_stream),
-                                   ctypes.c_void_p(self.copy_stream2.cuda_stream if self.copy_stream2 else None),
-                                   self.timeout_us))
+        if self.mode == "push":
+            if self.rank > 0:
+                # The previous rank writes into this B: announce when every
+                # earlier reader of it (on `stream`) has finished.
+                stream.synchronize()
+                self.recv_ok[self.rank] = epoch
+            if A is not None:
+                if self.rank == 0:
+                    kb.gemm(A, self.B, C, version=version, stream=stream)
+                else:
+                    kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, epoch, version=version, stream=stream)
+            nxt = self.rank + 1 < self.world
+            if nxt:
+                t0 = time.monotonic()
+                while self.recv_ok[self.rank + 1] != epoch:
+                    if time.monotonic() - t0 > self.timeout_s:
+                        raise kb.KebabError(kb.ETIMEOUT, "rank %d never became ready to receive" % (self.rank + 1))
+            kb.check(L.kebab_chain_push(
+                ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.next_b if nxt else None),
+                self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.next_ready if nxt else None), epoch,
+                ctypes.c_void_p(self._slot(self.rank) if self.rank > 0 else None),
+                ctypes.c_void_p(self._slot(self.rank + 1) if nxt else None), s1, s2, self.timeout_us))
+        else:
+            if self.rank == 0:
+                if A is not None:
+                    kb.gemm(A, self.B, C, version=version, stream=stream)
+                kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), None, self.chunk_bytes,
+                                           self.total_bytes, None, epoch, None, ctypes.c_void_p(self._slot(0)),
+                                           None, None, self.timeout_us))
+                return C
+            if A is not None:
+                kb.gemm_gated(A, self.B, C, self.ready, self.chunk_cols, epoch, version=version, stream=stream)
+            kb.check(L.kebab_ring_pull(ctypes.c_void_p(self.B.data_ptr()), ctypes.c_void_p(self.src_ptr),
+                                       self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
+                                       epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
+                                       ctypes.c_void_p(self._slot(self.rank)), s1, s2, self.timeout_us))
         stream.wait_stream(self.copy_stream)
         return C
 
     def close(self):
-        if self._src_handle is not None:
-            self.kb.check(self.kb.lib().kebab_ipc_close(self._src_handle))
-            self._src_handle = None
-        self.slots = None
+        for hb in self._opened:
+            self.kb.check(self.kb.lib().kebab_ipc_close(hb))
+        self._opened = []
+        self.slots = self.recv_ok = None
         self._anchor = None
         if getattr(self, "_mm", None) is not None:
             self._mm.close()

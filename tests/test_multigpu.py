@@ -34,7 +34,7 @@ if os.environ.get("KB_CHAIN"):
     from kebab_b200.shard import ChainBroadcastGemm
     a = shard_a(A, blk).contiguous()
     C = torch.empty((N, blk.rows), dtype=A.dtype, device=dev)
-    chain = ChainBroadcastGemm(B, chunk_cols=512)
+    chain = ChainBroadcastGemm(B, chunk_cols=512, mode=os.environ["KB_CHAIN"])
     for rep in range(2):  # the second call re-sends B over the same chain
         chain.run(a, C, version=int(os.environ["KB_VERSION"]))
         torch.cuda.synchronize()
@@ -103,8 +103,8 @@ def test_sharded_serpentine_within_tolerance(cuda, version):
     assert rel <= 1e-3, line
 
 
-@pytest.mark.parametrize("version", [105, 107])
-def test_chain_broadcast_gemm_bitexact(cuda, version):
-    """B pulled down the rank chain by copy engines while each rank's gated
+@pytest.mark.parametrize("version,mode", [(105, "push"), (107, "push"), (107, "pull")])
+def test_chain_broadcast_gemm_bitexact(cuda, version, mode):
+    """B moved down the rank chain by copy engines while each rank's gated
     GEMM runs: the gathered C equals one GPU's bit for bit."""
-    assert "RESULT bitexact" in _run(version, "", "0", chain="1")
+    assert "RESULT bitexact" in _run(version, "", "0", chain=mode)
