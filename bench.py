@@ -537,7 +537,7 @@ class Extras:
             out["broadcast_gbs"] = 2.0 * S * S / (out["broadcast_ms"] * 1e-3) / 1e9
             out["broadcast_plus_gemm_ms"] = sorted(one(True) for _ in range(3))[1]
             out["broadcast_plus_gemm_tflops"] = 2.0 * S ** 3 / (out["broadcast_plus_gemm_ms"] * 1e-3) / 1e12
-            cols = int(os.environ.get("KEBAB_BENCH_CHAIN_COLS", "0")) or (1024 if self.world <= 2 else 512)
+            cols = int(os.environ.get("KEBAB_BENCH_CHAIN_COLS", "0")) or 1024
             out["overlapped"] = self.chained(A, B, C, chunk_cols=cols, flops=2.0 * S ** 3, mode="push")
             out["overlapped_pull"] = self.chained(A, B, C, chunk_cols=cols, flops=2.0 * S ** 3, mode="pull")
         else:

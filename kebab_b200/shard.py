@@ -159,7 +159,7 @@ class ChainBroadcastGemm:
     written; the others are overwritten by every call). Collective: every
     rank constructs it and calls run() with the same shapes."""
 
-    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=2, mode="push"):
+    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=1, mode="push"):
         import ctypes
         import mmap
         import uuid
