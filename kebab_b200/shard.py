@@ -157,9 +157,13 @@ class ChainBroadcastGemm:
 
     `B` is this rank's [N, K] buffer (rank 0's holds the data and is never
     written; the others are overwritten by every call). Collective: every
-    rank constructs it and calls run() with the same shapes."""
+    rank constructs it and calls run() with the same shapes.
 
-    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=1, mode="push"):
+    `lib` replaces the C ABI (tests drive the host protocol on gloo ranks
+    with CPU buffers and a stand-in for the copy and IPC calls); on CPU
+    buffers there are no streams and run() takes A = None only."""
+
+    def __init__(self, B, chunk_cols=None, group=None, timeout_s=20.0, copy_streams=1, mode="push", lib=None):
         import ctypes
         import mmap
         import uuid
@@ -186,9 +190,11 @@ class ChainBroadcastGemm:
         self.timeout_us = int(timeout_s * 1e6)
         self.ready = torch.zeros(self.nchunks, dtype=torch.int32, device=B.device)
         self.epoch = 0
-        self.copy_stream = torch.cuda.Stream(device=B.device)
-        self.copy_stream2 = torch.cuda.Stream(device=B.device) if copy_streams > 1 else None
-        L = kb.lib()
+        cuda = B.is_cuda
+        self.copy_stream = torch.cuda.Stream(device=B.device) if cuda else None
+        self.copy_stream2 = torch.cuda.Stream(device=B.device) if cuda and copy_streams > 1 else None
+        self.lib = lib or kb.lib()
+        L = self.lib
 
         def export(t):
             h = (ctypes.c_char * 64)()
@@ -250,21 +256,26 @@ class ChainBroadcastGemm:
         import ctypes
         import time
         torch, kb = self.torch, self.kb
-        stream = stream or torch.cuda.current_stream()
+        cuda = self.B.is_cuda
+        if not cuda and A is not None:
+            raise ShardError("CPU buffers: broadcast only (A must be None)")
+        stream = stream or (torch.cuda.current_stream() if cuda else None)
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
         epoch = self.epoch
-        L = kb.lib()
-        s1 = ctypes.c_void_p(self.copy_stream.cuda_stream)
+        L = self.lib
+        s1 = ctypes.c_void_p(self.copy_stream.cuda_stream if cuda else None)
         s2 = ctypes.c_void_p(self.copy_stream2.cuda_stream if self.copy_stream2 else None)
         # This call's copies overwrite B: after every earlier use of B on `stream`.
-        self.copy_stream.wait_stream(stream)
-        if self.copy_stream2 is not None:
-            self.copy_stream2.wait_stream(stream)
+        if cuda:
+            self.copy_stream.wait_stream(stream)
+            if self.copy_stream2 is not None:
+                self.copy_stream2.wait_stream(stream)
         if self.mode == "push":
             if self.rank > 0:
                 # The previous rank writes into this B: announce when every
                 # earlier reader of it (on `stream`) has finished.
-                stream.synchronize()
+                if cuda:
+                    stream.synchronize()
                 self.recv_ok[self.rank] = epoch
             if A is not None:
                 if self.rank == 0:
@@ -296,12 +307,13 @@ class ChainBroadcastGemm:
                                        self.chunk_bytes, self.total_bytes, ctypes.c_void_p(self.ready.data_ptr()),
                                        epoch, ctypes.c_void_p(self._slot(self.rank - 1)),
                                        ctypes.c_void_p(self._slot(self.rank)), s1, s2, self.timeout_us))
-        stream.wait_stream(self.copy_stream)
+        if cuda:
+            stream.wait_stream(self.copy_stream)
         return C
 
     def close(self):
         for hb in self._opened:
-            self.kb.check(self.kb.lib().kebab_ipc_close(hb))
+            self.kb.check(self.lib.kebab_ipc_close(hb))
         self._opened = []
         self.slots = self.recv_ok = None
         self._anchor = None
