@@ -47,6 +47,7 @@ KEBAB_DECLARE_RUNG(gemm_v108_tma_umma_tmem_warpspecialized_persistent_streamk)  
 KEBAB_DECLARE_RUNG(gemm_v109_tma_umma_tmem_warpspecialized_persistent_2cta_streamk)  // v105 + stream-K
 KEBAB_DECLARE_RUNG(gemm_v110_tma_umma_tmem_warpspecialized_persistent_128x128)  // v104, 128 x 128 tiles
 KEBAB_DECLARE_RUNG(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64)   // v104, 128 x 64 tiles
+KEBAB_DECLARE_RUNG(gemm_v112_tma_umma_tmem_warpspecialized_persistent_2cta_256x384)  // pairs, 256 x 384 tiles
 KEBAB_DECLARE_RUNG(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c)  // v105, row-major C
 #undef KEBAB_DECLARE_RUNG
 

@@ -55,7 +55,7 @@ int kebab_flag_write(uint32_t* flag, uint32_t value, kebab_stream_t stream);
  * (a multiple of the rung's tile width: 512 for rung 107, 256 for 104 and
  * 105), and a tile needing chunk j waits (bounded, the kernel wait budget)
  * until b_ready[j] == epoch. Flags must be raised in chunk order. The
- * version must resolve to a persistent rung (104, 105, 107), else
+ * version must resolve to a persistent rung (104, 105, 107, 112), else
  * KEBAB_ENOTSUP. */
 int kebab_gemm_gated(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t M, int64_t N, int64_t K,
                      int version, const uint32_t* b_ready, int64_t chunk_cols, uint32_t epoch,

@@ -21,7 +21,7 @@ LIB_PATH = os.environ.get("KEBAB_B200_LIB") or os.path.join(PKG, "lib", "libkeba
 
 F16, BF16, F32 = 0, 1, 2
 OK, EINVAL, ENOTSUP, ECUDA, ETIMEOUT, ESPARSE = 0, 22, 95, 1001, 1002, 1003
-RUNGS = (1, 101, 102, 103, 104, 105, 106, 107, 108, 109, 110, 111, 141)
+RUNGS = (1, 101, 102, 103, 104, 105, 106, 107, 108, 109, 110, 111, 112, 141)
 HEURISTIC = 120
 # Reference version ids and the B200 rung each one maps to.
 REFERENCE_ID_MAP = {2: 102, 3: 102, 17: 102, 4: 103, 15: 103, 5: 104, 6: 104, 7: 104, 13: 104, 14: 104,

@@ -40,7 +40,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 
 REPO = Path(__file__).resolve().parents[1]
 DEFAULT_BENCH = REPO / "kebab_b200" / "bin" / "bench_gemm"
-V120_MODES = ("heuristic", "dp", "persistent", "pair", "wide", "streamk", "streamk1", "skinny", "n128", "n64")
+V120_MODES = ("heuristic", "dp", "persistent", "pair", "wide", "pair384", "streamk", "streamk1", "skinny", "n128", "n64")
 
 Problem = Tuple[int, int, int]
 
@@ -265,7 +265,7 @@ def main(argv: Optional[Sequence[str]] = None) -> int:
     ap.add_argument("--precisions", default="float16")
     ap.add_argument("--sizes", default="2048,4096,8192")
     ap.add_argument("--shapes", default="", help="extra problems, MxNxK comma separated")
-    ap.add_argument("--v120-modes", default="heuristic,pair,wide,streamk")
+    ap.add_argument("--v120-modes", default="heuristic,pair,wide,pair384,streamk")
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--measurement", type=int, default=40)
     ap.add_argument("--top-k", type=int, default=10)

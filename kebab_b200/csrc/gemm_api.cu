@@ -43,6 +43,7 @@ const Rung kRungs[] = {
     {109, "tma_umma_tmem_warpspecialized_persistent_2cta_streamk", launch_v109_pair_streamk},
     {110, "tma_umma_tmem_warpspecialized_persistent_128x128", launch_v110_persistent_n128},
     {111, "tma_umma_tmem_warpspecialized_persistent_128x64", launch_v111_persistent_n64},
+    {112, "tma_umma_tmem_warpspecialized_persistent_2cta_256x384", launch_v112_pair_384},
     {141, "tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c", launch_v105_pair},
 };
 
@@ -71,7 +72,7 @@ int map_reference_id(int v) {
 // decomposition from the tile count against the QUERIED SM count.
 // KEBAB_V120_MODE = dp | persistent | pair | wide | streamk (pairs) | streamk1
 // (1-CTA) | n128 | n64 | skinny | heuristic (default).
-int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
+int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc, bool rhs_kmajor) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
     std::string m(env);
@@ -80,6 +81,7 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
     if (m == "PERSISTENT") return 104;
     if (m == "PAIR" || m == "2CTA") return 105;
     if (m == "WIDE" || m == "PAIRWIDE") return 107;
+    if (m == "PAIR384" || m == "FIT") return 112;
     if (m == "STREAMK" || m == "PAIRSTREAMK") return 109;
     if (m == "STREAMK1") return 108;
     if (m == "N128" || m == "NARROW") return 110;
@@ -92,20 +94,28 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc) {
   // on 111) the small-problem tiles below win.
   if (M <= 256 && rc_colc && N * K >= (int64_t)4 * 1024 * 1024) return 106;
   const int64_t pairs = sm_count / 2;
-  const int64_t wide_tiles = ((M + 255) / 256) * ((N + 511) / 512);
   const int64_t pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  // 256 x 512 pair tiles cut operand traffic per FLOP by a quarter (lower
-  // power, higher clock under the cap) and beat 256 x 256 tiles by ~5 % per
-  // tile; worth it with at least one full wave, no N padding and a last-wave
-  // fill within 5 points of the 256 x 256 tiling's (4096^3: 128 wide tiles on
-  // 74 pairs fill 86 % like 256 pair tiles do, and run at 1396 TFLOP/s
-  // against 1336 for rung 105 and 1321 for rung 109).
-  auto fill = [pairs](int64_t t) { return (double)t / (double)(((t + pairs - 1) / pairs) * pairs); };
-  if (N % 512 == 0 && wide_tiles >= pairs && fill(wide_tiles) >= fill(pair_tiles) - 0.05) return 107;
   // Pair tiles halve B traffic per CTA; worth it once they fill the pairs.
-  // The stream-K rungs (108, 109) are not chosen here: measured against
-  // 105 they tie at 4096^3 and lose at 3072 x 2048 x 2048 (828 vs 953).
-  if (pair_tiles >= pairs) return 105;
+  // Among the pair widths 256 (105), 512 (107, N a multiple of 512) and 384
+  // (112, column-major B only) take the least cost = waves x tile width x a
+  // per-FLOP factor: wider tiles stage fewer operand bytes per FLOP (lower
+  // power, higher clock under the cap), 256 wide ~5 % slower per FLOP than
+  // 512 and 384 ~2 %. Measured (TFLOP/s, 105 / 107 / 112): 4096^3 1326 /
+  // 1397 / 1251, 3072^3 1319 / 1363 / 1057, 3072 x 2048 x 2048 913 / 896 /
+  // 1101, 2048 x 3072 x 4096 1063 / 1097 / 1269, 2560 x 8192 x 4096 1349 /
+  // 1268 / 1411. The stream-K rungs (108, 109) are not chosen here: measured
+  // against 105 they tie at 4096^3 and lose at 3072 x 2048 x 2048 (828 vs 953).
+  if (pair_tiles >= pairs) {
+    auto cost = [&](int bn, double per_flop) {
+      const int64_t t = ((M + 255) / 256) * ((N + bn - 1) / bn);
+      return (double)((t + pairs - 1) / pairs) * bn * per_flop;
+    };
+    int best = 105;
+    double c = cost(256, 1.05);
+    if (N % 512 == 0 && cost(512, 1.0) <= c) best = 107, c = cost(512, 1.0);
+    if (rhs_kmajor && cost(384, 1.02) < 0.97 * c) best = 112;
+    return best;
+  }
   // Small problems: the widest 128-row tiles that still occupy the SMs.
   // 128 x 256 (v104) at 2048^3 and 4096 x 1024 x 1024; 128 x 128 (v110) at
   // 1280^3 .. 1536^3 and 2048 x 1024 x 4096; 128 x 64 (v111, latency-bound
@@ -148,13 +158,13 @@ int kebab_list_versions(int* out, int cap) {
   return n;
 }
 
-static int resolve(int version, int64_t M, int64_t N, int64_t K, bool rc_colc) {
+static int resolve(int version, int64_t M, int64_t N, int64_t K, bool rc_colc, bool rhs_kmajor = true) {
   int id = map_reference_id(version);
   if (id == 120) {
     DeviceInfo* d = nullptr;
     int rc = device_info(&d);
     int sms = rc == KEBAB_OK ? d->sm_count : 148;
-    id = choose_v120(M, N, K, sms, rc_colc);
+    id = choose_v120(M, N, K, sms, rc_colc, rhs_kmajor);
   }
   if (!find_rung(id)) {
     fail(KEBAB_EINVAL, "unsupported version " + std::to_string(version));
@@ -184,7 +194,7 @@ int kebab_gemm(kebab_dtype dtype, const void* A, const void* B, void* C, int64_t
   if ((lhs != 'R' && lhs != 'C') || (rhs != 'R' && rhs != 'C') || (cl != 'R' && cl != 'C') || mode.size() > 3)
     return fail(KEBAB_EINVAL, "opmode must be two (or three, with C's layout) of R/C, got \"" + mode + "\"");
   const bool c_row = (cl == 'R') || map_reference_id(version) == 141;
-  const int id = resolve(version, M, N, K, lhs == 'R' && rhs == 'C' && !c_row);
+  const int id = resolve(version, M, N, K, lhs == 'R' && rhs == 'C' && !c_row, rhs == 'C');
   if (id < 0) return -id;
   const Rung* r = find_rung(id);
   GemmProblem p{(int)dtype, A, B, C, M, N, K, lhs, rhs, c_row, reinterpret_cast<cudaStream_t>(stream)};
@@ -199,8 +209,8 @@ int kebab_gemm_gated(kebab_dtype dtype, const void* A, const void* B, void* C, i
   if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "gated GEMM supports F16 and BF16");
   const int id = resolve(version, M, N, K, true);
   if (id < 0) return -id;
-  if (id != 104 && id != 105 && id != 107)
-    return fail(KEBAB_ENOTSUP, "gated B runs on the persistent rungs 104, 105 and 107; version " +
+  if (id != 104 && id != 105 && id != 107 && id != 112)
+    return fail(KEBAB_ENOTSUP, "gated B runs on the persistent rungs 104, 105, 107 and 112; version " +
                                    std::to_string(version) + " resolves to " + std::to_string(id));
   GemmProblem p{(int)dtype, A, B, C, M, N, K, 'R', 'C', false, reinterpret_cast<cudaStream_t>(stream)};
   p.b_ready = b_ready;
@@ -259,6 +269,7 @@ KEBAB_RUNG_LAUNCHER(gemm_v108_tma_umma_tmem_warpspecialized_persistent_streamk, 
 KEBAB_RUNG_LAUNCHER(gemm_v109_tma_umma_tmem_warpspecialized_persistent_2cta_streamk, 109)
 KEBAB_RUNG_LAUNCHER(gemm_v110_tma_umma_tmem_warpspecialized_persistent_128x128, 110)
 KEBAB_RUNG_LAUNCHER(gemm_v111_tma_umma_tmem_warpspecialized_persistent_128x64, 111)
+KEBAB_RUNG_LAUNCHER(gemm_v112_tma_umma_tmem_warpspecialized_persistent_2cta_256x384, 112)
 KEBAB_RUNG_LAUNCHER(gemm_v141_tma_umma_tmem_warpspecialized_persistent_2cta_rowmajor_c, 141)
 #undef KEBAB_RUNG_LAUNCHER
 

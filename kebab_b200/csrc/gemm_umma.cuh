@@ -255,6 +255,23 @@ struct UmmaSmem {
 };
 
 enum : int { LAYOUT_A_MN = 1, LAYOUT_B_MN = 2, LAYOUT_C_ROW = 4 };
+#define B_MN_OF(layout) (((layout) & LAYOUT_B_MN) != 0)
+
+// Global column of accumulator column d of a tile starting at column n0.
+// With two sub-MMAs (BN = 384 / 512, CTA pairs) each CTA of the pair holds
+// BN/2 contiguous B rows and sub-MMA s takes H = BN/4 of them from each: its
+// accumulator columns [2Hs, 2Hs + H) are the leader's rows n0 + Hs + [0, H)
+// and [2Hs + H, 2H(s+1)) the peer's rows n0 + BN/2 + Hs + [0, H).
+template <int BN, int NSUB>
+__device__ __forceinline__ int pair_col(int n0, int d) {
+  if constexpr (NSUB == 1) {
+    return n0 + d;
+  } else {
+    constexpr int H = BN / 4;
+    const int s = d / (2 * H), r = d % (2 * H);
+    return n0 + (r >= H ? BN / 2 : 0) + H * s + (r % H);
+  }
+}
 
 // Operand descriptor for k-step `k` (16 elements of K) of a staged tile.
 template <bool MN>
@@ -270,11 +287,14 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   using L = UmmaSmem<BN, STAGES, CG>;
   constexpr int BM_T = 128 * CG;  // rows per (pair) tile
   constexpr int TMEM_COLS = 512;
-  // BN = 512 (pairs only): two N = 256 MMAs per k-step share the A tile; the
-  // 512-column accumulator fills TMEM, so it is single-buffered.
-  constexpr int NSUB = BN / 256 > 1 ? BN / 256 : 1;
+  // BN = 384 or 512 (pairs only): two N = BN/2 MMAs per k-step share the A
+  // tile; the accumulator takes more than half of TMEM, so it is
+  // single-buffered. Sub-MMA s reads rows [s BN/4, (s+1) BN/4) of each CTA's
+  // B tile (see pair_col for where its columns land in C).
+  constexpr int NSUB = BN > 256 ? 2 : 1;
   constexpr int ACCS = (2 * BN <= TMEM_COLS) ? 2 : 1;
-  static_assert(BN <= 256 || (BN == 512 && CG == 2), "BN = 512 needs CTA pairs");
+  static_assert(BN <= 256 || ((BN == 384 || BN == 512) && CG == 2), "BN = 384 / 512 needs CTA pairs");
+  static_assert(BN != 384 || !B_MN_OF(LAYOUT), "BN = 384 needs column-major (K-major) B");
   static_assert(!SK || (PERSISTENT && BN <= 256), "stream-K needs the persistent 4-warp epilogue");
   constexpr bool A_MN = (LAYOUT & LAYOUT_A_MN) != 0;
   constexpr bool B_MN = (LAYOUT & LAYOUT_B_MN) != 0;
@@ -452,12 +472,12 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
             const uint64_t ad = operand_desc<A_MN>(a_addr, k);
 #pragma unroll
             for (int sub = 0; sub < NSUB; ++sub) {
-              // Sub-MMA `sub` reads rows [128 sub, 128 sub + 128) of each CTA's B tile.
-              const uint64_t bd = operand_desc<B_MN>(b_addr + sub * (128 * L::BK * 2), k);
+              // Sub-MMA `sub` reads rows [sub BN/4, (sub+1) BN/4) of each CTA's B tile.
+              const uint64_t bd = operand_desc<B_MN>(b_addr + sub * ((BN / 4) * L::BK * 2), k);
               if constexpr (CG == 1)
-                umma_f16_cg1(d_tmem + sub * 256, ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
+                umma_f16_cg1(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
               else
-                umma_f16_cg2(d_tmem + sub * 256, ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
+                umma_f16_cg2(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
             }
           }
           any_issued = true;
@@ -574,8 +594,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           __syncwarp();
           if (lane == 0) {
             const int d = c * 32;
-            const int gcol = NSUB == 1 ? n0 + d : n0 + ((d & 255) >= 128 ? 256 : 0) + 128 * (d >> 8) + (d & 127);
-            tma_store_2d(&tmC, buf, m_rows, gcol);
+            tma_store_2d(&tmC, buf, m_rows, pair_col<BN, NSUB>(n0, d));
             tma_store_commit();
           }
           ++sub;
@@ -641,7 +660,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           // the pair holds 256 contiguous B rows, so sub-MMA s covers columns
           // n0 + 128 s + [0, 128) (leader) and n0 + 256 + 128 s + [0, 128) (peer).
           const int d = c * 32;
-          const int gcol = NSUB == 1 ? n0 + d : n0 + ((d & 255) >= 128 ? 256 : 0) + 128 * (d >> 8) + (d & 127);
+          const int gcol = pair_col<BN, NSUB>(n0, d);
           if constexpr (!C_ROW) tma_store_2d(&tmC, buf, m_rows, gcol);
           else tma_store_2d(&tmC, buf, gcol, m_rows);
           tma_store_commit();

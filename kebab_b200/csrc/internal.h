@@ -81,6 +81,7 @@ int launch_v108_streamk(const GemmProblem& p);
 int launch_v109_pair_streamk(const GemmProblem& p);
 int launch_v110_persistent_n128(const GemmProblem& p);
 int launch_v111_persistent_n64(const GemmProblem& p);
+int launch_v112_pair_384(const GemmProblem& p);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Clock probe armed by kebab_clock_probe() on this host thread for the next

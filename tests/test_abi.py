@@ -101,7 +101,9 @@ def test_v120_heuristic_without_gpu():
     assert r(8192, 8192, 8192) == 107 and r(4096, 4096, 8192) == 107 and r(4096, 4096, 4096) == 107
     assert r(16384, 28672, 8192) == 107
     assert r(4096, 3840, 4096) == 105     # N % 512 != 0: 256 x 256 pair tiles
-    assert r(2560, 8192, 4096) == 105     # wide tiles fill the last wave worse
+    assert r(2560, 8192, 4096) == 112     # 256 x 384 pair tiles: 3 waves against 5 (256) and 3 (512)
+    assert r(3072, 2048, 2048) == 112 and r(2048, 3072, 4096) == 112  # one wave of 256 x 384
+    assert r(3072, 3072, 3072) == 107     # 72 wide tiles: one wave on 74 pairs
     assert r(64, 8192, 8192) == 106 and r(128, 4096, 4096) == 106 and r(64, 2048, 2048) == 106
     assert r(256, 1024, 1024) == 111      # too little of B for the skinny rung
     assert r(2048, 2048, 2048) == 104 and r(4096, 1024, 1024) == 104

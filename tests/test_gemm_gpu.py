@@ -11,7 +11,7 @@ from gemm_util import assert_close, inputs, run
 
 pytestmark = pytest.mark.gpu
 
-TC_RUNGS = [101, 102, 103, 104, 105, 107, 110, 111]
+TC_RUNGS = [101, 102, 103, 104, 105, 107, 110, 111, 112]
 ALL_RUNGS = [1] + TC_RUNGS
 
 
@@ -34,7 +34,7 @@ def test_ragged_shapes(cuda, version, shape):
     assert_close(run(A, B, M, N, K, O.F16, version, cuda), ref, "v%d %s" % (version, shape))
 
 
-@pytest.mark.parametrize("version", [103, 104, 105, 107, 120])
+@pytest.mark.parametrize("version", [103, 104, 105, 107, 112, 120])
 @pytest.mark.parametrize("dtype", [O.F16, O.BF16])
 def test_2048_full(cuda, version, dtype):
     M = N = K = 2048

@@ -44,9 +44,23 @@ def _run(cuda, M, N, K, opmode, version, dtype=O.F16, seed=0):
 
 
 @pytest.mark.parametrize("opmode", ["RC", "RR", "CR", "CC", "RCR", "RRR", "CRR", "CCR"])
-@pytest.mark.parametrize("version", [1, 103, 104, 105, 107, 108, 109, 110, 111, 120])
+@pytest.mark.parametrize("version", [1, 103, 104, 105, 107, 108, 109, 110, 111, 112, 120])
 def test_layouts(cuda, opmode, version):
+    if version == 112 and opmode[1] == "R":
+        # rung 112 takes column-major B only, and says so
+        import torch
+        import kebab_b200 as kb
+        p = torch.empty(1 << 20, dtype=torch.float16, device=cuda)
+        assert kb.gemm_raw(0, p.data_ptr(), p.data_ptr(), p.data_ptr(), 384, 512, 320, opmode, 112,
+                           torch.cuda.current_stream().cuda_stream) == kb.ENOTSUP
+        return
     _run(cuda, 384, 512, 320, opmode, version)
+
+
+@pytest.mark.parametrize("opmode", ["RC", "CC", "RCR", "CCR"])
+def test_v112_two_waves_ragged(cuda, opmode):
+    """256 x 384 pair tiles: several tiles per pair, ragged N (last tile 1/3 full), both C layouts."""
+    _run(cuda, 3072, 2176, 448, opmode, 112)
 
 
 @pytest.mark.parametrize("opmode", ["RR", "CC", "RCR"])

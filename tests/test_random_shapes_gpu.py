@@ -14,7 +14,7 @@ from gemm_util import assert_close, inputs, run
 
 pytestmark = pytest.mark.gpu
 
-RUNGS = [103, 104, 105, 106, 107, 108, 109, 110, 111, 120]
+RUNGS = [103, 104, 105, 106, 107, 108, 109, 110, 111, 112, 120]
 
 
 def _shapes(n, seed):
