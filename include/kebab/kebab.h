@@ -83,7 +83,7 @@ int kebab_device_status(kebab_stream_t stream, uint32_t* code, int clear);
  * the KEBAB_WAIT_TIMEOUT_MS environment variable). */
 int kebab_set_wait_timeout_us(uint64_t timeout_us);
 
-/* Arms a clock probe for the next tcgen05 GEMM launch (dense rungs 103-111,
+/* Arms a clock probe for the next tcgen05 GEMM launch (dense rungs 103-112,
  * 141, and the 2:4 sparse GEMM) made by this host thread: thread 0 of every
  * CTA of that launch writes four uint64 at buf[4 * cta]: the SM cycle counter
  * and the global nanosecond timer at entry, then both again at exit.

@@ -50,9 +50,10 @@ int kebab_ipc_close(const void* handle);
  * kernel (a stream memory operation), after all earlier work on `stream`. */
 int kebab_flag_write(uint32_t* flag, uint32_t value, kebab_stream_t stream);
 
-/* GEMM (RC, column-major C; same arguments and rung choice as kebab_gemm)
- * whose B is still arriving: B's columns come in chunks of `chunk_cols`
- * (a multiple of the rung's tile width: 512 for rung 107, 256 for 104 and
+/* GEMM (RC, column-major C; same arguments as kebab_gemm, and the same rung
+ * choice except that the heuristic never picks rung 112 here) whose B is
+ * still arriving: B's columns come in chunks of `chunk_cols` (a multiple of
+ * the rung's tile width: 512 for rung 107, 384 for 112, 256 for 104 and
  * 105), and a tile needing chunk j waits (bounded, the kernel wait budget)
  * until b_ready[j] == epoch. Flags must be raised in chunk order. The
  * version must resolve to a persistent rung (104, 105, 107, 112), else

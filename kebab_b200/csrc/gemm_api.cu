@@ -72,7 +72,7 @@ int map_reference_id(int v) {
 // decomposition from the tile count against the QUERIED SM count.
 // KEBAB_V120_MODE = dp | persistent | pair | wide | streamk (pairs) | streamk1
 // (1-CTA) | n128 | n64 | skinny | heuristic (default).
-int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc, bool rhs_kmajor) {
+int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc, bool allow_384) {
   const char* env = std::getenv("KEBAB_V120_MODE");
   if (env && *env) {
     std::string m(env);
@@ -113,7 +113,7 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc, boo
     int best = 105;
     double c = cost(256, 1.05);
     if (N % 512 == 0 && cost(512, 1.0) <= c) best = 107, c = cost(512, 1.0);
-    if (rhs_kmajor && cost(384, 1.02) < 0.97 * c) best = 112;
+    if (allow_384 && cost(384, 1.02) < 0.97 * c) best = 112;
     return best;
   }
   // Small problems: the widest 128-row tiles that still occupy the SMs.
@@ -158,13 +158,14 @@ int kebab_list_versions(int* out, int cap) {
   return n;
 }
 
-static int resolve(int version, int64_t M, int64_t N, int64_t K, bool rc_colc, bool rhs_kmajor = true) {
+// allow_384: rung 112 may be chosen (column-major B, no 512-column chunking).
+static int resolve(int version, int64_t M, int64_t N, int64_t K, bool rc_colc, bool allow_384 = true) {
   int id = map_reference_id(version);
   if (id == 120) {
     DeviceInfo* d = nullptr;
     int rc = device_info(&d);
     int sms = rc == KEBAB_OK ? d->sm_count : 148;
-    id = choose_v120(M, N, K, sms, rc_colc, rhs_kmajor);
+    id = choose_v120(M, N, K, sms, rc_colc, allow_384);
   }
   if (!find_rung(id)) {
     fail(KEBAB_EINVAL, "unsupported version " + std::to_string(version));
@@ -207,7 +208,8 @@ int kebab_gemm_gated(kebab_dtype dtype, const void* A, const void* B, void* C, i
   if (!A || !B || !C || !b_ready) return fail(KEBAB_EINVAL, "null pointer passed to kebab_gemm_gated");
   if (M <= 0 || N <= 0 || K <= 0) return fail(KEBAB_EINVAL, "invalid dimensions");
   if (dtype != KEBAB_F16 && dtype != KEBAB_BF16) return fail(KEBAB_EINVAL, "gated GEMM supports F16 and BF16");
-  const int id = resolve(version, M, N, K, true);
+  // The heuristic keeps to widths that divide the 512-aligned chunks callers use.
+  const int id = resolve(version, M, N, K, true, false);
   if (id < 0) return -id;
   if (id != 104 && id != 105 && id != 107 && id != 112)
     return fail(KEBAB_ENOTSUP, "gated B runs on the persistent rungs 104, 105, 107 and 112; version " +
