@@ -99,21 +99,24 @@ int choose_v120(int64_t M, int64_t N, int64_t K, int sm_count, bool rc_colc, boo
   // Among the pair widths 256 (105), 512 (107, N a multiple of 512) and 384
   // (112, column-major B only) take the least cost = waves x tile width x a
   // per-FLOP factor: wider tiles stage fewer operand bytes per FLOP (lower
-  // power, higher clock under the cap), 256 wide ~5 % slower per FLOP than
-  // 512 and 384 ~2 %. Measured (TFLOP/s, 105 / 107 / 112): 4096^3 1326 /
-  // 1397 / 1251, 3072^3 1319 / 1363 / 1057, 3072 x 2048 x 2048 913 / 896 /
-  // 1101, 2048 x 3072 x 4096 1063 / 1097 / 1269, 2560 x 8192 x 4096 1349 /
-  // 1268 / 1411. The stream-K rungs (108, 109) are not chosen here: measured
-  // against 105 they tie at 4096^3 and lose at 3072 x 2048 x 2048 (828 vs 953).
+  // power, higher clock under the cap). Fitted factors from the measurements
+  // below: 256 wide 1.05-1.11 (the upper end in power-capped loops), 384
+  // 0.99-1.06, against 512 = 1. Measured (TFLOP/s, 105 / 107 / 112):
+  // 4096^3 1326 / 1397 / 1251, 3072^3 1319 / 1363 / 1057, 3072 x 2048 x 2048
+  // 913 / 896 / 1101, 2048 x 3072 x 4096 1063 / 1097 / 1269, 2560 x 8192 x
+  // 4096 1349 / 1268 / 1411, 2048 x 28672 x 8192 (config 4a on 8 GPUs) 1272
+  // / 1315 / 1296. The stream-K rungs (108, 109) are not chosen here:
+  // measured against 105 they tie at 4096^3, lose at 3072 x 2048 x 2048 (828
+  // vs 953) and at 2048 x 28672 x 8192 (1261 vs 1272).
   if (pair_tiles >= pairs) {
     auto cost = [&](int bn, double per_flop) {
       const int64_t t = ((M + 255) / 256) * ((N + bn - 1) / bn);
       return (double)((t + pairs - 1) / pairs) * bn * per_flop;
     };
     int best = 105;
-    double c = cost(256, 1.05);
+    double c = cost(256, 1.08);
     if (N % 512 == 0 && cost(512, 1.0) <= c) best = 107, c = cost(512, 1.0);
-    if (allow_384 && cost(384, 1.02) < 0.97 * c) best = 112;
+    if (allow_384 && cost(384, 1.03) < 0.97 * c) best = 112;
     return best;
   }
   // Small problems: the widest 128-row tiles that still occupy the SMs.

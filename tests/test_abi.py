@@ -100,6 +100,7 @@ def test_v120_heuristic_without_gpu():
     r = lambda M, N, K: kb.lib().kebab_resolve_version(120, kb.F16, M, N, K)
     assert r(8192, 8192, 8192) == 107 and r(4096, 4096, 8192) == 107 and r(4096, 4096, 4096) == 107
     assert r(16384, 28672, 8192) == 107
+    assert r(2048, 28672, 8192) == 107 and r(4096, 28672, 8192) == 107  # config 4a shards on 8 / 4 GPUs
     assert r(4096, 3840, 4096) == 105     # N % 512 != 0: 256 x 256 pair tiles
     assert r(2560, 8192, 4096) == 112     # 256 x 384 pair tiles: 3 waves against 5 (256) and 3 (512)
     assert r(3072, 2048, 2048) == 112 and r(2048, 3072, 4096) == 112  # one wave of 256 x 384
