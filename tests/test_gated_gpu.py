@@ -14,7 +14,7 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("version,M,N,K,chunk", [(107, 1024, 4096, 2048, 1024), (105, 768, 2560, 1024, 512),
-                                                 (104, 512, 3072, 512, 768)])
+                                                 (104, 512, 3072, 512, 768), (112, 768, 2688, 1024, 768)])
 def test_gated_equals_ungated(cuda, version, M, N, K, chunk):
     import torch
     import kebab_b200 as kb
