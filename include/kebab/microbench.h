@@ -43,6 +43,15 @@ int kebab_mbench_tmem_ld(int iters, double* bytes_per_clk_per_sm, double* tbps);
  * device buffer [rows][cols] FP16 split across all SMs: GB/s. */
 int kebab_mbench_tma_load(const void* buf, int64_t rows, int64_t cols, int box_rows, double* gbps);
 
+/* The tma_load loop over a buffer small enough to stay in L2 (first read by
+ * an untimed pass), read `passes` times with `stages` boxes of box_rows x 64
+ * FP16 in flight per SM (1..8, at most 200 KB): aggregate GB/s and bytes per
+ * SM cycle (median CTA). Shows how much operand data one SM can take in per
+ * cycle, and how that depends on the bytes it keeps in flight. Variant of
+ * the reference's TMA bandwidth probe (copy_gmem_to_smem_2d_tma_ptx.cu). */
+int kebab_mbench_tma_ingest(const void* buf, int64_t rows, int64_t cols, int box_rows, int stages, int passes,
+                            double* gbps, double* bytes_per_clk_per_sm);
+
 #ifdef __cplusplus
 }
 #endif

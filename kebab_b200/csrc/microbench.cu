@@ -12,6 +12,8 @@
 //                bandwidth per SM.
 //   tma_load     each CTA streams a slice of a large global buffer through a
 //                shared-memory ring with 2-D TMA loads: TMA / HBM read bandwidth.
+//   tma_ingest   the same loop over an L2-resident slice, several passes, with
+//                a chosen ring depth: bytes one SM takes in per cycle.
 // A TMA-multicast probe is not built: multicast loads are kept out of every
 // source file so that the library may run on several GPUs of this pool.
 // Every wait is bounded (ptx.cuh).
@@ -203,10 +205,14 @@ __global__ void __launch_bounds__(128, 1) tmem_ld_kernel(int iters, long long* c
 }
 
 // Streams rows [blockIdx.x * rows_per_cta, ...) of a [rows][cols] FP16 array
-// through STAGES shared-memory slots of box_rows x 64 elements.
+// through STAGES shared-memory slots of box_rows x 64 elements, `passes`
+// times over (passes > 1 with a slice that stays in L2 measures what one SM
+// can take in from L2). Thread 0 of each CTA records its SM cycles from the
+// first load to the last arrival in cycles[blockIdx.x] when cycles != null.
 constexpr int TMA_STAGES = 8;  // slots allocated; `stages` of them are used
 __global__ void __launch_bounds__(64, 1) tma_load_kernel(const __grid_constant__ CUtensorMap tm, int rows_per_cta,
-                                                         int box_rows, int col_boxes, int stages, WaitCtx ctx) {
+                                                         int box_rows, int col_boxes, int stages, int passes,
+                                                         long long* cycles, WaitCtx ctx) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* s = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int stage_bytes = box_rows * 128;
@@ -218,7 +224,9 @@ __global__ void __launch_bounds__(64, 1) tma_load_kernel(const __grid_constant__
   __syncthreads();
   if (threadIdx.x != 0) return;
   const int row0 = blockIdx.x * rows_per_cta;
-  const int nboxes = (rows_per_cta / box_rows) * col_boxes;
+  const int per_pass = (rows_per_cta / box_rows) * col_boxes;
+  const int nboxes = per_pass * passes;
+  const long long t0 = clock64();
   // Keep `stages` loads in flight; the "consumer" only waits for arrival.
   for (int i = 0; i < nboxes + stages; ++i) {
     if (i >= stages) {
@@ -226,11 +234,12 @@ __global__ void __launch_bounds__(64, 1) tma_load_kernel(const __grid_constant__
       if (!mbar_wait(&full[j % stages], (uint32_t)((j / stages) & 1), ctx, SITE_FULL)) return;
     }
     if (i < nboxes) {
-      const int st = i % stages;
+      const int st = i % stages, b = i % per_pass;
       mbar_arrive_expect_tx(&full[st], stage_bytes);
-      tma_load_2d(s + st * stage_bytes, &tm, &full[st], (i % col_boxes) * 64, row0 + (i / col_boxes) * box_rows);
+      tma_load_2d(s + st * stage_bytes, &tm, &full[st], (b % col_boxes) * 64, row0 + (b / col_boxes) * box_rows);
     }
   }
+  if (cycles) cycles[blockIdx.x] = clock64() - t0;
 }
 
 struct Events {
@@ -448,14 +457,62 @@ int kebab_mbench_tma_load(const void* buf, int64_t rows, int64_t cols, int box_r
   cudaError_t e = cudaFuncSetAttribute(tma_load_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
   Events ev;
-  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, ctx);
+  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, 1, nullptr, ctx);
   if ((rc = finish(nullptr, "tma_load warm-up"))) return rc;
   cudaEventRecord(ev.a);
-  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, ctx);
+  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, 1, nullptr, ctx);
   cudaEventRecord(ev.b);
   if ((rc = finish(nullptr, "tma_load"))) return rc;
   *gbps = (double)rows_per_cta * grid * cols * 2.0 / (ev.ms() * 1e-3) / 1e9;
   return KEBAB_OK;
+}
+
+int kebab_mbench_tma_ingest(const void* buf, int64_t rows, int64_t cols, int box_rows, int stages, int passes,
+                            double* gbps, double* bytes_per_clk_per_sm) {
+  if (!buf || rows <= 0 || cols <= 0 || cols % 64 || box_rows <= 0 || box_rows > 256 || box_rows % 8 || !gbps ||
+      !bytes_per_clk_per_sm || passes <= 0 || stages < 1 || stages > TMA_STAGES || stages * box_rows * 128 > 200 * 1024)
+    return fail(KEBAB_EINVAL, "tma_ingest: cols % 64 == 0, box_rows a multiple of 8 in 8..256, 1..8 stages of at "
+                              "most 200 KB in all, passes > 0");
+  DeviceInfo* dev = nullptr;
+  int rc = device_info(&dev);
+  if (rc) return rc;
+  WaitCtx ctx;
+  if ((rc = wait_ctx(&ctx))) return rc;
+  const int grid = dev->sm_count;
+  const int64_t rows_per_cta = (rows / grid) / box_rows * box_rows;
+  if (rows_per_cta <= 0) return fail(KEBAB_EINVAL, "tma_ingest: buffer too small for one box per SM");
+  if ((rows_per_cta / box_rows) * (cols / 64) * passes > INT32_MAX) return fail(KEBAB_EINVAL, "tma_ingest: too many boxes");
+  CUtensorMap tm;
+  if ((rc = make_tmap_2d(&tm, buf, KEBAB_F16, rows, cols, cols, box_rows, 64, true))) return rc;
+  const int smem = 1024 + stages * box_rows * 128 + 8 * stages + 64;
+  cudaError_t e = cudaFuncSetAttribute(tma_load_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  long long* cyc = nullptr;
+  if ((e = cudaMalloc(&cyc, sizeof(long long) * grid)) != cudaSuccess) return cuda_fail(e, "cudaMalloc");
+  Events ev;
+  // One pass brings the slices into L2; the timed launch then reads them `passes` times.
+  tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, 1, nullptr, ctx);
+  rc = finish(nullptr, "tma_ingest warm-up");
+  if (!rc) {
+    cudaEventRecord(ev.a);
+    tma_load_kernel<<<grid, 64, smem>>>(tm, (int)rows_per_cta, box_rows, (int)(cols / 64), stages, passes, cyc, ctx);
+    cudaEventRecord(ev.b);
+    rc = finish(nullptr, "tma_ingest");
+  }
+  if (!rc) {
+    std::vector<long long> h(grid);
+    e = cudaMemcpy(h.data(), cyc, sizeof(long long) * grid, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "cudaMemcpy");
+    } else {
+      std::sort(h.begin(), h.end());
+      const double bytes_cta = (double)rows_per_cta * cols * 2.0 * passes;
+      *gbps = bytes_cta * grid / (ev.ms() * 1e-3) / 1e9;
+      *bytes_per_clk_per_sm = bytes_cta / (double)h[grid / 2];
+    }
+  }
+  cudaFree(cyc);
+  return rc;
 }
 
 }  // extern "C"

@@ -21,6 +21,8 @@ def _L():
     L.kebab_mbench_umma_sp.argtypes = [c.c_int, c.c_int, c.c_int, c.POINTER(c.c_double), c.POINTER(c.c_double)]
     L.kebab_mbench_tmem_ld.argtypes = [c.c_int, c.POINTER(c.c_double), c.POINTER(c.c_double)]
     L.kebab_mbench_tma_load.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_int, c.POINTER(c.c_double)]
+    L.kebab_mbench_tma_ingest.argtypes = [c.c_void_p, c.c_int64, c.c_int64, c.c_int, c.c_int, c.c_int,
+                                          c.POINTER(c.c_double), c.POINTER(c.c_double)]
     return L
 
 
@@ -64,6 +66,15 @@ def tma_load(buf, box_rows=128):
     return g.value
 
 
+def tma_ingest(buf, box_rows=128, stages=6, passes=20):
+    """L2-resident TMA loads: (aggregate GB/s, bytes per SM cycle)."""
+    rows, cols = buf.shape
+    g, b = ctypes.c_double(), ctypes.c_double()
+    kb.check(_L().kebab_mbench_tma_ingest(ctypes.c_void_p(buf.data_ptr()), rows, cols, box_rows, stages, passes,
+                                          ctypes.byref(g), ctypes.byref(b)))
+    return g.value, b.value
+
+
 def run_all():
     import torch
     out = {}
@@ -86,6 +97,15 @@ def run_all():
     buf = torch.empty((1 << 16, 16384), dtype=torch.float16, device="cuda")  # 2 GiB, > L2
     for box in (64, 128, 256):
         out["tma_load_box%d_gbs" % box] = tma_load(buf, box)
+    del buf
+    small = torch.empty((148 * 256, 512), dtype=torch.float16, device="cuda")  # 37 MiB, stays in L2
+    for box in (128, 256):
+        for stages in (1, 2, 3, 4, 6):
+            if stages * box * 128 > 200 * 1024:
+                continue
+            g, b = tma_ingest(small, box, stages)
+            out["tma_ingest_box%d_stages%d" % (box, stages)] = {"gbs": g, "bytes_per_clk_per_sm": b,
+                                                                 "bytes_in_flight": stages * box * 128}
     return out
 
 

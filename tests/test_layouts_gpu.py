@@ -51,7 +51,7 @@ def test_layouts(cuda, opmode, version):
         import torch
         import kebab_b200 as kb
         p = torch.empty(1 << 20, dtype=torch.float16, device=cuda)
-        assert kb.gemm_raw(0, p.data_ptr(), p.data_ptr(), p.data_ptr(), 384, 512, 320, opmode, 112,
+        assert kb.gemm_raw(0, p.data_ptr(), p.data_ptr(), p.data_ptr(), 384, 512, 320, opmode, version,
                            torch.cuda.current_stream().cuda_stream) == kb.ENOTSUP
         return
     _run(cuda, 384, 512, 320, opmode, version)

@@ -37,6 +37,22 @@ def test_latency_tmem_tma(cuda):
         assert 500 < gbs < 12000, (box, gbs)
 
 
+def test_tma_ingest_l2(cuda):
+    """L2-resident TMA loads: the per-SM intake rises with the bytes in flight
+    and stays within physical bounds (the figure is derived from SM cycles)."""
+    import torch
+    from kebab_b200 import microbench as mb
+    small = torch.ones((148 * 256, 512), dtype=torch.float16, device=cuda)  # 37 MiB, stays in L2
+    g1, b1 = mb.tma_ingest(small, 128, 1, passes=4)
+    g4, b4 = mb.tma_ingest(small, 128, 4, passes=4)
+    assert 0.5 < b1 < 1024 and 0.5 < b4 < 1024, (b1, b4)
+    assert 100 < g1 < 200000 and 100 < g4 < 200000, (g1, g4)
+    assert b4 > b1, (b1, b4)
+    import kebab_b200 as kb
+    with pytest.raises(kb.KebabError):
+        mb.tma_ingest(small, 128, 9)  # more than 8 slots
+
+
 @pytest.mark.parametrize("cg", [1, 2])
 def test_umma_sparse_throughput(cuda, cg):
     """tcgen05.mma.sp issue rate: on CTA pairs at N = 256 the 2:4 MMA runs at
