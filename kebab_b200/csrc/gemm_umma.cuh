@@ -236,12 +236,16 @@ struct UmmaEpi {
   static constexpr int THREADS = 64 + 32 * WARPS;
 };
 
-template <int BN, int STAGES, int CG>
+// A stage holds KPS sub-tiles of 64 K (one 128-byte swizzle row each) of A
+// and of B: a ring slot and its barrier per KPS K-blocks.
+template <int BN, int STAGES, int CG, int KPS = 1>
 struct UmmaSmem {
   static constexpr int BM = 128;  // rows of A per CTA
   static constexpr int BK = 64;   // 64 x 2 bytes = one 128-byte swizzle row
-  static constexpr int A_STAGE = BM * BK * 2;
-  static constexpr int B_STAGE = (BN / CG) * BK * 2;
+  static constexpr int A_SUB = BM * BK * 2;
+  static constexpr int B_SUB = (BN / CG) * BK * 2;
+  static constexpr int A_STAGE = KPS * A_SUB;
+  static constexpr int B_STAGE = KPS * B_SUB;
   static constexpr int C_SUB = 32 * 32 * 2;  // one 32x32 staging sub-tile
   static constexpr int C_BYTES = UmmaEpi<BN>::WARPS * 2 * C_SUB;
   static constexpr int OFF_A = 0;
@@ -280,11 +284,14 @@ __device__ __forceinline__ uint64_t operand_desc(uint32_t base, int k) {
   else return umma_desc_sw128(base + k * 32);                          // 16 K elements = 32 bytes
 }
 
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0, bool SK = false>
+// KPS: K-blocks of 64 per ring stage (2: half as many barrier round trips per
+// byte; each stage then carries 2 A and 2 B boxes).
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT = 0, bool SK = false, int KPS = 1>
 __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
     gemm_umma_ws_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmC, const UmmaArgs args) {
-  using L = UmmaSmem<BN, STAGES, CG>;
+  using L = UmmaSmem<BN, STAGES, CG, KPS>;
+  static_assert(KPS == 1 || !SK, "stream-K splits single K-blocks");
   constexpr int BM_T = 128 * CG;  // rows per (pair) tile
   constexpr int TMEM_COLS = 512;
   // BN = 384 or 512 (pairs only): two N = BN/2 MMAs per k-step share the A
@@ -360,7 +367,7 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
   const int num_tiles = args.tiles_m * args.tiles_n;
   const int cluster_id = blockIdx.x / CG;
   const int num_clusters = gridDim.x / CG;
-  const int num_kb = (args.K + L::BK - 1) / L::BK;
+  const int num_kb = (args.K + L::BK * KPS - 1) / (L::BK * KPS);  // ring stages per tile
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -404,25 +411,29 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           uint8_t* sB = smem + L::OFF_B + stage * L::B_STAGE;
           // K-major tiles are one box (x = K, y = rows); MN-major tiles are
           // boxes of 64 rows-or-columns each (x = M or N, y = K).
-          auto load = [&](uint8_t* dst, const CUtensorMap* tm, int rows0, int nrows, bool mn, int hint) {
+          // kq: index of the 64-wide K-block within K.
+          auto load = [&](uint8_t* dst, const CUtensorMap* tm, int rows0, int nrows, bool mn, int hint, int kq) {
             if (!mn && hint) {
               const uint64_t pol = hint == 1 ? l2_policy_evict_last()
                                    : hint == 2 ? l2_policy_evict_first() : l2_policy_evict_normal();
-              if constexpr (CG == 1) tma_load_2d_hint(dst, tm, &full[stage], kb * L::BK, rows0, pol);
-              else tma_load_2d_pair_hint(dst, tm, full_leader0 + stage * 8u, kb * L::BK, rows0, pol);
+              if constexpr (CG == 1) tma_load_2d_hint(dst, tm, &full[stage], kq * L::BK, rows0, pol);
+              else tma_load_2d_pair_hint(dst, tm, full_leader0 + stage * 8u, kq * L::BK, rows0, pol);
             } else if (!mn) {
-              if constexpr (CG == 1) tma_load_2d(dst, tm, &full[stage], kb * L::BK, rows0);
-              else tma_load_2d_pair(dst, tm, full_leader0 + stage * 8u, kb * L::BK, rows0);
+              if constexpr (CG == 1) tma_load_2d(dst, tm, &full[stage], kq * L::BK, rows0);
+              else tma_load_2d_pair(dst, tm, full_leader0 + stage * 8u, kq * L::BK, rows0);
             } else {
               for (int j = 0; j < nrows / 64; ++j) {
-                if constexpr (CG == 1) tma_load_2d(dst + j * 8192, tm, &full[stage], rows0 + j * 64, kb * L::BK);
-                else tma_load_2d_pair(dst + j * 8192, tm, full_leader0 + stage * 8u, rows0 + j * 64, kb * L::BK);
+                if constexpr (CG == 1) tma_load_2d(dst + j * 8192, tm, &full[stage], rows0 + j * 64, kq * L::BK);
+                else tma_load_2d_pair(dst + j * 8192, tm, full_leader0 + stage * 8u, rows0 + j * 64, kq * L::BK);
               }
             }
           };
           if (CG == 1 || leader) mbar_arrive_expect_tx(&full[stage], TX_BYTES);
-          load(sA, &tmA, m0, 128, A_MN, args.l2_hint & 3);
-          load(sB, &tmB, n0, BN / CG, B_MN, (args.l2_hint >> 2) & 3);
+#pragma unroll
+          for (int q = 0; q < KPS; ++q) {
+            load(sA + q * L::A_SUB, &tmA, m0, 128, A_MN, args.l2_hint & 3, kb * KPS + q);
+            load(sB + q * L::B_SUB, &tmB, n0, BN / CG, B_MN, (args.l2_hint >> 2) & 3, kb * KPS + q);
+          }
           issued[stage] = true;
           issued_parity[stage] = phase;
           if (++stage == STAGES) {
@@ -468,16 +479,20 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
           const uint32_t a_addr = smem_u32(smem + L::OFF_A + stage * L::A_STAGE);
           const uint32_t b_addr = smem_u32(smem + L::OFF_B + stage * L::B_STAGE);
 #pragma unroll
-          for (int k = 0; k < L::BK / 16; ++k) {
-            const uint64_t ad = operand_desc<A_MN>(a_addr, k);
+          for (int q = 0; q < KPS; ++q) {
 #pragma unroll
-            for (int sub = 0; sub < NSUB; ++sub) {
-              // Sub-MMA `sub` reads rows [sub BN/4, (sub+1) BN/4) of each CTA's B tile.
-              const uint64_t bd = operand_desc<B_MN>(b_addr + sub * ((BN / 4) * L::BK * 2), k);
-              if constexpr (CG == 1)
-                umma_f16_cg1(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
-              else
-                umma_f16_cg2(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, (i != 0 || k != 0) ? 1u : 0u);
+            for (int k = 0; k < L::BK / 16; ++k) {
+              const uint64_t ad = operand_desc<A_MN>(a_addr + q * L::A_SUB, k);
+              const uint32_t acc_flag = (i != 0 || q != 0 || k != 0) ? 1u : 0u;
+#pragma unroll
+              for (int sub = 0; sub < NSUB; ++sub) {
+                // Sub-MMA `sub` reads rows [sub BN/4, (sub+1) BN/4) of each CTA's B tile.
+                const uint64_t bd = operand_desc<B_MN>(b_addr + q * L::B_SUB + sub * ((BN / 4) * L::BK * 2), k);
+                if constexpr (CG == 1)
+                  umma_f16_cg1(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, acc_flag);
+                else
+                  umma_f16_cg2(d_tmem + sub * (BN / NSUB), ad, bd, IDESC, acc_flag);
+              }
             }
           }
           any_issued = true;

@@ -13,9 +13,9 @@
 namespace kb {
 namespace umma_launch {
 
-template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT, bool SK = false>
+template <typename T, int BN, int STAGES, int CG, bool PERSISTENT, int LAYOUT, bool SK = false, int KPS = 1>
 int launch_umma(const GemmProblem& p) {
-  using L = UmmaSmem<BN, STAGES, CG>;
+  using L = UmmaSmem<BN, STAGES, CG, KPS>;
   int rc = check_tma_shapes(p);
   if (rc) return rc;
   DeviceInfo* dev = nullptr;
@@ -79,7 +79,7 @@ int launch_umma(const GemmProblem& p) {
   const long long tiles = (long long)args.tiles_m * args.tiles_n;
   if (tiles > INT32_MAX / 2) return fail(KEBAB_EINVAL, "too many tiles");
 
-  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>;
+  auto kern = gemm_umma_ws_kernel<T, BN, STAGES, CG, PERSISTENT, LAYOUT, SK, KPS>;
   // Once per device and instantiation: the shared-memory opt-in and, for
   // pairs (which must be co-resident on a GPC), how many clusters fit.
   static std::once_flag attr_once[64];
@@ -200,26 +200,26 @@ int launch_umma(const GemmProblem& p) {
 
 
 
-template <int CG, bool PERSISTENT, int STAGES, int LAYOUT, int BN, bool SK>
+template <int CG, bool PERSISTENT, int STAGES, int LAYOUT, int BN, bool SK, int KPS = 1>
 int dispatch_dtype(const GemmProblem& p) {
-  if (p.dtype == KEBAB_F16) return launch_umma<__half, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>(p);
-  return launch_umma<__nv_bfloat16, BN, STAGES, CG, PERSISTENT, LAYOUT, SK>(p);
+  if (p.dtype == KEBAB_F16) return launch_umma<__half, BN, STAGES, CG, PERSISTENT, LAYOUT, SK, KPS>(p);
+  return launch_umma<__nv_bfloat16, BN, STAGES, CG, PERSISTENT, LAYOUT, SK, KPS>(p);
 }
 
 // Layout from the problem: A column-major, B row-major, C row-major bits.
-template <int CG, bool PERSISTENT, int STAGES, int BN = 256, bool SK = false>
+template <int CG, bool PERSISTENT, int STAGES, int BN = 256, bool SK = false, int KPS = 1>
 int dispatch(const GemmProblem& p) {
   const int layout = (p.lhs == 'C' ? LAYOUT_A_MN : 0) | (p.rhs == 'R' ? LAYOUT_B_MN : 0) |
                      (p.c_row ? LAYOUT_C_ROW : 0);
   switch (layout) {
-    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0, BN, SK>(p);
-    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1, BN, SK>(p);
-    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2, BN, SK>(p);
-    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3, BN, SK>(p);
-    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4, BN, SK>(p);
-    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5, BN, SK>(p);
-    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6, BN, SK>(p);
-    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7, BN, SK>(p);
+    case 0: return dispatch_dtype<CG, PERSISTENT, STAGES, 0, BN, SK, KPS>(p);
+    case 1: return dispatch_dtype<CG, PERSISTENT, STAGES, 1, BN, SK, KPS>(p);
+    case 2: return dispatch_dtype<CG, PERSISTENT, STAGES, 2, BN, SK, KPS>(p);
+    case 3: return dispatch_dtype<CG, PERSISTENT, STAGES, 3, BN, SK, KPS>(p);
+    case 4: return dispatch_dtype<CG, PERSISTENT, STAGES, 4, BN, SK, KPS>(p);
+    case 5: return dispatch_dtype<CG, PERSISTENT, STAGES, 5, BN, SK, KPS>(p);
+    case 6: return dispatch_dtype<CG, PERSISTENT, STAGES, 6, BN, SK, KPS>(p);
+    default: return dispatch_dtype<CG, PERSISTENT, STAGES, 7, BN, SK, KPS>(p);
   }
 }
 

@@ -82,6 +82,8 @@ int launch_v109_pair_streamk(const GemmProblem& p);
 int launch_v110_persistent_n128(const GemmProblem& p);
 int launch_v111_persistent_n64(const GemmProblem& p);
 int launch_v112_pair_384(const GemmProblem& p);
+// K-blocks per ring stage: KEBAB_KPS=1 or 2 (read per call), else `dflt`.
+int kps_env(int dflt);
 int launch_v106_skinny_splits(const GemmProblem& p, int splits);  // splits <= 0: heuristic
 
 // Clock probe armed by kebab_clock_probe() on this host thread for the next

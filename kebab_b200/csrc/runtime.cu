@@ -107,6 +107,13 @@ int wait_ctx(WaitCtx* out) {
   return KEBAB_OK;
 }
 
+int kps_env(int dflt) {
+  const char* e = std::getenv("KEBAB_KPS");
+  if (e && e[0] == '1') return 1;
+  if (e && e[0] == '2') return 2;
+  return dflt;
+}
+
 bool pdl_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("KEBAB_PDL");

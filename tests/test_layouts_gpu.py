@@ -63,6 +63,15 @@ def test_v112_two_waves_ragged(cuda, opmode):
     _run(cuda, 3072, 2176, 448, opmode, 112)
 
 
+@pytest.mark.parametrize("kps", ["1", "2"])
+@pytest.mark.parametrize("opmode", ["RC", "RR", "CC", "CRR"])
+def test_v105_ring_shapes(cuda, opmode, kps, monkeypatch):
+    """Rung 105's two rings (6 stages of one K-block, 3 stages of two):
+    K = 200 ends inside the second K-block of a stage, ragged M and N."""
+    monkeypatch.setenv("KEBAB_KPS", kps)
+    _run(cuda, 520, 776, 200, opmode, 105)
+
+
 @pytest.mark.parametrize("opmode", ["RR", "CC", "RCR"])
 def test_layouts_ragged_and_bf16(cuda, opmode):
     _run(cuda, 264, 520, 136, opmode, 105)
