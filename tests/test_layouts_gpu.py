@@ -63,13 +63,14 @@ def test_v112_two_waves_ragged(cuda, opmode):
     _run(cuda, 3072, 2176, 448, opmode, 112)
 
 
+@pytest.mark.parametrize("version", [105, 110, 111])
 @pytest.mark.parametrize("kps", ["1", "2"])
 @pytest.mark.parametrize("opmode", ["RC", "RR", "CC", "CRR"])
-def test_v105_ring_shapes(cuda, opmode, kps, monkeypatch):
-    """Rung 105's two rings (6 stages of one K-block, 3 stages of two):
-    K = 200 ends inside the second K-block of a stage, ragged M and N."""
+def test_ring_shapes(cuda, opmode, kps, version, monkeypatch):
+    """The rungs' two rings (one K-block per stage, or two): K = 200 ends
+    inside the second K-block of a stage, ragged M and N."""
     monkeypatch.setenv("KEBAB_KPS", kps)
-    _run(cuda, 520, 776, 200, opmode, 105)
+    _run(cuda, 520, 776, 200, opmode, version)
 
 
 @pytest.mark.parametrize("opmode", ["RR", "CC", "RCR"])
