@@ -698,7 +698,9 @@ __global__ void __launch_bounds__(UmmaEpi<BN>::THREADS, 1)
         acc_phase ^= 1u;
       }
     }
-    if (lane == 0) tma_store_wait_all<0>();
+    // The CTA may exit once its last C stores have read their staging
+    // buffers; the global writes complete with the grid.
+    if (lane == 0) tma_store_wait_read<0>();
     __syncwarp();
   }
 
