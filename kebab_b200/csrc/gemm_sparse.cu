@@ -186,7 +186,9 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
 #pragma unroll
           for (int t = 0; t < MT; ++t) {
             const int m0 = mb * BM_T + t * BM_MMA + (int)rank * 128;
-            const int e_row = (m0 / 128) * num_kb * 128 + kb * 128;
+            // E block (m-block, k-block) is 2 KB of contiguous bytes: rows of
+            // 128 bytes in the tensor map, 16 per block.
+            const int e_row = ((m0 / 128) * num_kb + kb) * 16;
             if constexpr (CG == 1) {
               tma_load_2d(sA + t * L::A_TILE, &tmA, &full[stage], kb * 64, m0);
               tma_load_2d(sE + t * L::E_TILE, &tmE, &full[stage], 0, e_row);
@@ -379,10 +381,12 @@ __global__ void __launch_bounds__(SparseCfg<T, CG, STAGES, MT, BN>::THREADS, 1)
   probe.end(args.clk);
 }
 
-// E viewed as a 2-D array of uint16: 8 per 16-byte row, 128 rows per block.
+// E viewed as a 2-D array of uint16 with 128-byte rows (64 per row), 16 rows
+// per 2 KB block: one block is 16 row copies for the TMA unit rather than 128
+// copies of 16 bytes.
 int make_tmap_e(CUtensorMap* out, const void* E, int64_t M, int64_t K) {
-  const uint64_t rows = (uint64_t)(M / 128) * (uint64_t)(K / 128) * 128;
-  return make_tmap_2d(out, E, KEBAB_F16, rows, 8, 8, 128, 8, false);
+  const uint64_t rows = (uint64_t)(M / 128) * (uint64_t)(K / 128) * 16;
+  return make_tmap_2d(out, E, KEBAB_F16, rows, 64, 64, 16, 64, false);
 }
 
 template <typename T, int CG, int STAGES, int MT, int BN>
