@@ -59,6 +59,7 @@ struct SkinnySmem {
   static constexpr int BYTES = AREA + TAIL;
   static constexpr int ALLOC = BYTES + 1024;
   static constexpr bool FITS = ALLOC <= 232448;
+  static_assert(FITS, "shared memory budget exceeded");
   static constexpr int PER_SM = (2 * ALLOC + 2048 <= 233472) ? 2 : 1;
 };
 
